@@ -1,0 +1,463 @@
+"""Benchmark of the B200 decode-sampling step (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU)
+
+Headline workload: 1024 independent rows per GPU of
+V=49152 fp32 logits ~N(0,2^2) with Zipf(1.1) histories of 4096 int32 ids; the full
+sampling chain (repetition penalty, temperature 1.5, top-k 50, top-p 0.9, softmax,
+draw from a per-row uniform) in one fused launch per step.  Rows are sharded
+across ranks with no collective in the step ("weak" scaling: 1024 rows per GPU).
+Two input sets alternate between steps (2 x 218 MB > the 126 MB L2), so every
+step streams its inputs from HBM.
+
+Prints one JSON line (rank 0).  `value` is rows/s over all GPUs with inputs
+resident in HBM; `e2e` is the same metric through the C ABI from pinned host
+buffers (host->device copies of logits, histories and uniforms and the
+device->host read of the tokens inside the timed region); `roofline` relates the
+kernel's algorithmic bytes to the measured HBM copy bandwidth; `cpu_baseline`
+times the CPU port of the reference algorithm (oracle/) on a bounded sample.
+`extras` holds the latency configs (1, 2, 3) and the loop guard (config 5).
+
+--impl reference times only the CPU port of the reference's algorithm on this
+host's cores, on the same workload and metric (rank 0; other ranks exit).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+V = 49152
+ROWS = 1024
+HIST = 4096
+METRIC = "sampled rows/s at V=49152 (HBM GB/s vs peak); us per 2-beam decode step"
+WORKLOAD = "cfg4: 1024 rows/GPU x V=49152 fp32 N(0,2^2), Zipf(1.1) histories of 4096 int32 ids, T=1.5 top_k=50 top_p=0.9"
+
+# ------------------------------------------------------------------ workloads
+
+
+def history_with_repeats(rng, n, vocab, repeat_frac=0.3):
+    """n ids: (1 - repeat_frac) uniform in [0, vocab), the rest copies of earlier ids."""
+    ids = rng.integers(0, vocab, n)
+    rep = rng.random(n) < repeat_frac
+    rep[0] = False
+    src = (rng.random(n) * np.arange(n)).astype(np.int64)
+    for j in np.nonzero(rep)[0]:
+        ids[j] = ids[src[j]]
+    return ids.astype(np.int32)
+
+
+def zipf_ids(rng, shape, vocab, a=1.1):
+    """Zipf(a) ids over [0, vocab): numpy zipf resampled until <= vocab, id = x - 1."""
+    x = rng.zipf(a, size=shape)
+    bad = x > vocab
+    while bad.any():
+        x[bad] = rng.zipf(a, size=int(bad.sum()))
+        bad = x > vocab
+    return (x - 1).astype(np.int32)
+
+
+def to_bf16_values(x):
+    """Round float32 values to bfloat16 (nearest even), returned as float32."""
+    b = x.astype(np.float32).view(np.uint32)
+    b = ((b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return b.view(np.float32)
+
+
+def cfg1(seed=0, vocab=V):
+    """Config 1: B=1, 2*N(0,1) logits, 20 ids boosted +8, 1024-id history (30 % repeats)."""
+    rng = np.random.default_rng(seed)
+    x = (2.0 * rng.standard_normal((1, vocab))).astype(np.float32)
+    x[0, rng.choice(vocab, 20, replace=False)] += 8.0
+    hist = history_with_repeats(rng, 1024, vocab)[None]
+    u = rng.random(1).astype(np.float32)
+    return dict(logits=x, history=hist, uniforms=u, temperature=1.5, top_p=0.9, keep=1)
+
+
+def cfg2(seed=1, vocab=V, beams=2, hist_len=2048):
+    """Config 2: 2 beams, N(0,2^2) logits, 2048-id histories, running scores U(-200,-10)."""
+    rng = np.random.default_rng(seed)
+    x = (2.0 * rng.standard_normal((beams, vocab))).astype(np.float32)
+    hist = rng.integers(0, vocab, (beams, hist_len)).astype(np.int32)
+    running = rng.uniform(-200, -10, beams).astype(np.float32)
+    u = rng.random(2 * beams).astype(np.float32)
+    return dict(logits=x, history=hist, running=running, uniforms=u, temperature=1.5, top_p=0.9)
+
+
+def cfg3(seed=2, vocab=V, beams=8, hist_len=8000):
+    """Config 3: 8 beams, bf16 N(0,3^2) logits with 1 % of ids +6, 8000-id histories."""
+    rng = np.random.default_rng(seed)
+    x = (3.0 * rng.standard_normal((beams, vocab))).astype(np.float32)
+    x[:, rng.choice(vocab, vocab // 100, replace=False)] += 6.0
+    hist = rng.integers(0, vocab, (beams, hist_len)).astype(np.int32)
+    running = rng.uniform(-200, -10, beams).astype(np.float32)
+    u = rng.random(2 * beams).astype(np.float32)
+    return dict(logits=to_bf16_values(x), history=hist, running=running, uniforms=u, temperature=1.5, top_p=0.9)
+
+
+def cfg4(seed=3, rows=ROWS, vocab=V, hist_len=HIST):
+    """Config 4: rows x V N(0,2^2) fp32 logits, Zipf(1.1) histories of 4096 ids."""
+    rng = np.random.default_rng(seed)
+    x = (2.0 * rng.standard_normal((rows, vocab))).astype(np.float32)
+    hist = zipf_ids(rng, (rows, hist_len), vocab)
+    u = rng.random(rows).astype(np.float32)
+    return dict(logits=x, history=hist, uniforms=u, temperature=1.5, top_p=0.9, keep=1)
+
+
+def cfg5_tokens(seed=4, rows=256, length=16384, vocab=V, window=64, repeats=3):
+    """Config 5: loop-guard histories; rows [0, rows/2) end with one window repeated
+    `repeats` times (planted, non-overlapping), the other rows are random."""
+    rng = np.random.default_rng(seed)
+    t = rng.integers(0, vocab, (rows, length)).astype(np.int32)
+    for r in range(rows // 2):
+        win = rng.integers(0, vocab, window)
+        starts = np.sort(rng.choice((length - window) // window - 1, repeats - 1, replace=False)) * window
+        for s in starts:
+            t[r, s:s + window] = win
+        t[r, length - window:] = win
+    return t
+
+
+def row_bytes(vocab=V, hist=HIST, logit_bytes=4, id_bytes=4):
+    """Algorithmic bytes per row of one sampling step: logits + history ids + the
+    uniform read; token (8) + kept count (4) + status (4) written."""
+    return vocab * logit_bytes + hist * id_bytes + 4 + 8 + 4 + 4
+
+
+# ------------------------------------------------------------------ helpers
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every `period` seconds."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index, period=0.002):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period, self._stop, self._thread = period, threading.Event(), None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(self.period)
+
+    def sample(self):
+        if self.nvml is None:
+            return
+        try:
+            self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+            r = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._thread.join()
+        self.sample()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def cpu_port_rows_per_s(data, seconds=10.0, chunk=64):
+    """The CPU port of the reference algorithm (oracle/) on all host threads, on a
+    bounded sample: chunks of `chunk` rows of the workload until `seconds` pass."""
+    from oracle import oracle as O
+    x, h, u = data["logits"], data["history"], data["uniforms"]
+    n = x.shape[0]
+    t0 = time.perf_counter()
+    rows = 0
+    i = 0
+    while True:
+        s = slice(i, i + chunk)
+        O.sample(x[s], u[s], ids=h[s], temperature=1.5, top_p=0.9, cap=0)
+        rows += x[s].shape[0]
+        i = (i + chunk) % n
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return rows / dt, rows, dt
+
+
+# ------------------------------------------------------------------ reference arm
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    data = cfg4(rows=256)
+    from oracle import oracle as O
+    threads = os.cpu_count()
+    x, h, u = data["logits"], data["history"], data["uniforms"]
+    per_step = 256
+
+    def step():
+        O.sample(x, u, ids=h, temperature=1.5, top_p=0.9, cap=0, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = per_step * args.steps / dt
+    sample = f"{per_step} rows of the workload per step (CPU port of runtime_shared.py:170-202, oracle/)"
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "rows_per_step": per_step, "vocab": V, "history": HIST},
+            "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__
+    sv = __graft_entry__.load_package()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    sets = []
+    for s in range(2):
+        d = cfg4(seed=3 + 1000 * rank + s)
+        sets.append(dict(logits=torch.from_numpy(d["logits"]).to(dev), history=torch.from_numpy(d["history"]).to(dev),
+                         uniforms=torch.from_numpy(d["uniforms"]).to(dev), host=d))
+    outs = [dict(token=torch.empty(ROWS, dtype=torch.int64, device=dev),
+                 count=torch.empty(ROWS, dtype=torch.int32, device=dev),
+                 status=torch.empty(ROWS, dtype=torch.int32, device=dev)) for _ in range(2)]
+
+    def step(i):
+        d = sets[i & 1]
+        sv.sample_step(d["logits"], d["uniforms"], history=d["history"], temperature=1.5, top_p=0.9, top_k=50,
+                       keep=1, repetition_penalty=3.1, out=outs[i & 1])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    st = outs[0]["status"].max().item()
+    if st:
+        raise RuntimeError(f"sampling status {st}")
+    sampler = ClockSampler(local_rank)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(args.steps):
+            ev[2 * i].record(stream)
+            step(i)
+            ev[2 * i + 1].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = start.elapsed_time(end)
+    kern_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)]
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    rows_total = ROWS * world * args.steps
+    value = rows_total / (total_ms / 1e3)
+
+    # Roofline of the fused kernel: algorithmic bytes per launch / mean launch time.
+    per_launch = ROWS * row_bytes()
+    mean_kern_s = statistics.mean(kern_ms) / 1e3
+    achieved = per_launch / mean_kern_s / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # End to end through the C ABI from pinned host buffers (rank-local).
+    host_x = torch.from_numpy(sets[0]["host"]["logits"]).pin_memory()
+    host_h = torch.from_numpy(sets[0]["host"]["history"]).pin_memory()
+    host_u = torch.from_numpy(sets[0]["host"]["uniforms"]).pin_memory()
+    host_tok = torch.empty(ROWS, dtype=torch.int64).pin_memory()
+    dx = torch.empty_like(sets[0]["logits"])
+    dh = torch.empty_like(sets[0]["history"])
+    du = torch.empty_like(sets[0]["uniforms"])
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        dx.copy_(host_x, non_blocking=True)
+        dh.copy_(host_h, non_blocking=True)
+        du.copy_(host_u, non_blocking=True)
+        o = sv.sample_step(dx, du, history=dh, temperature=1.5, top_p=0.9, out=outs[0])
+        host_tok.copy_(o["token"], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = ROWS * world * e2e_steps / (e2e_ms / 1e3)
+    h2d = host_x.numel() * 4 + host_h.numel() * 4 + host_u.numel() * 4
+    d2h = ROWS * 8
+
+    extras = latency_extras(sv, dev) if rank == 0 and not args.no_extras else {}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rps, rows, dt = cpu_port_rows_per_s(sets[0]["host"], seconds=args.cpu_seconds)
+        cpu = {"value": rps, "unit": "rows/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{rows} rows of the workload in {dt:.1f} s (oracle/ C port, OpenMP over rows)"}
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "vocab": V, "history_ids": HIST,
+                           "parallelism": f"row-sharded x{world}, no collective in the step",
+                           "l2": "two alternating input sets of 218 MB each (> 126 MB L2)"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None,
+                             "peak_source": peak_kind, "algorithmic_bytes_per_launch": per_launch,
+                             "mean_launch_us": mean_kern_s * 1e6},
+                "cpu_baseline": cpu,
+                "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "gpu_launches": args.steps,
+                "clocks": sampler.summary(),
+                "extras": extras}
+        print(json.dumps(line), flush=True)
+
+
+def graph_time_us(fn, reps=200):
+    """Mean device time of fn() replayed from a CUDA graph (after warm-up)."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(10):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / reps
+
+
+def latency_extras(sv, dev):
+    import torch
+    out = {}
+    d = cfg1()
+    x, h, u = (torch.from_numpy(d[k]).to(dev) for k in ("logits", "history", "uniforms"))
+    o1 = {}
+    sv.sample_step(x, u, history=h, out=o1, dense="probs")
+    out["cfg1_us_per_step"] = graph_time_us(lambda: sv.sample_step(x, u, history=h, out=o1, dense="probs"))
+    for name, gen, dt in (("cfg2_beam2_us_per_step", cfg2, torch.float32),
+                          ("cfg3_beam8_bf16_us_per_step", cfg3, torch.bfloat16)):
+        d = gen()
+        x = torch.from_numpy(d["logits"]).to(dev).to(dt)
+        h = torch.from_numpy(d["history"]).to(dev)
+        rs = torch.from_numpy(d["running"]).to(dev)
+        u = torch.from_numpy(d["uniforms"]).to(dev)
+        ob = {}
+        sv.beam_step(x, rs, u, history=h, out=ob)
+        out[name] = graph_time_us(lambda: sv.beam_step(x, rs, u, history=h, out=ob))
+    t = torch.from_numpy(cfg5_tokens()).to(dev)
+    lens = torch.full((t.shape[0],), t.shape[1], dtype=torch.int32, device=dev)
+    v = torch.empty(t.shape[0], dtype=torch.uint8, device=dev)
+    sv.loop_guard(t, lens, out=v)
+    out["cfg5_loop_guard_us"] = graph_time_us(lambda: sv.loop_guard(t, lens, out=v))
+    out["cfg5_loop_guard_GBps"] = t.numel() * 4 / (out["cfg5_loop_guard_us"] * 1e-6) / 1e9
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-extras", action="store_true", help="skip the latency configs")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,111 @@
+// sv_loop_guard.cu -- batched loop guard (runtime_shared.py:156-167, _repeating).
+//
+// Verdict for a row of L tokens: L >= window*repeats and the last `window` tokens
+// occur at least `repeats` times (overlapping starts allowed, the tail itself
+// counted).  One CTA per row.  Tokens are staged chunk by chunk in shared memory;
+// each thread owns a contiguous run of window starts and rolls a polynomial hash
+// (mod 2^64, odd base) along it; a start whose hash equals the tail's hash is
+// verified token by token, so the verdict is exact.  The scan stops once
+// `repeats` occurrences are found.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "sv_internal.h"
+
+namespace sv {
+
+constexpr int LG_NT = 256;
+constexpr int LG_PER = 17;                  // starts per thread (odd: no bank conflicts)
+constexpr int LG_CH = LG_NT * LG_PER;       // starts per chunk
+constexpr int LG_MAXW = 1024;               // window limit
+constexpr uint64_t LG_BASE = 0x9E3779B97F4A7C15ull;
+
+template <typename Tok>
+__global__ void __launch_bounds__(LG_NT) loop_guard_kernel(const Tok* __restrict__ tokens, int64_t stride,
+                                                           const int32_t* __restrict__ lengths, int window,
+                                                           int repeats, uint8_t* __restrict__ verdict) {
+  extern __shared__ __align__(16) unsigned char lg_smem[];
+  Tok* buf = reinterpret_cast<Tok*>(lg_smem);                       // LG_CH + window - 1
+  Tok* tail = buf + LG_CH + LG_MAXW;                                 // window
+  __shared__ int count;
+  __shared__ unsigned long long htail, bpow;
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x;
+  int64_t L = lengths[row];
+  if (stride > 0 && L > stride) L = stride;  // a row holds at most `stride` tokens
+  const Tok* t = tokens + row * stride;
+  if (L < (int64_t)window * repeats) {
+    if (tid == 0) verdict[row] = 0;
+    return;
+  }
+  for (int j = tid; j < window; j += LG_NT) tail[j] = t[L - window + j];
+  if (tid == 0) count = 0;
+  __syncthreads();
+  if (tid == 0) {
+    uint64_t h = 0, p = 1;
+    for (int j = 0; j < window; ++j) {
+      h = h * LG_BASE + (uint64_t)(int64_t)tail[j];
+      if (j) p *= LG_BASE;
+    }
+    htail = h;
+    bpow = p;  // LG_BASE^(window-1)
+  }
+  __syncthreads();
+  const uint64_t ht = htail, bp = bpow;
+  const int64_t nstarts = L - window + 1;
+  for (int64_t c0 = 0; c0 < nstarts; c0 += LG_CH) {
+    const int64_t cn = nstarts - c0 < LG_CH ? nstarts - c0 : LG_CH;
+    const int64_t ntok = cn + window - 1;
+    for (int64_t j = tid; j < ntok; j += LG_NT) buf[j] = t[c0 + j];
+    __syncthreads();
+    const int s0 = tid * LG_PER;
+    if (s0 < cn) {
+      uint64_t h = 0;
+      for (int j = 0; j < window; ++j) h = h * LG_BASE + (uint64_t)(int64_t)buf[s0 + j];
+      const int s1 = s0 + LG_PER < cn ? s0 + LG_PER : (int)cn;
+      for (int s = s0; s < s1; ++s) {
+        if (s > s0) h = (h - (uint64_t)(int64_t)buf[s - 1] * bp) * LG_BASE + (uint64_t)(int64_t)buf[s + window - 1];
+        if (h == ht) {
+          bool eq = true;
+          for (int j = 0; j < window && eq; ++j) eq = buf[s + j] == tail[j];
+          if (eq) atomicAdd(&count, 1);
+        }
+      }
+    }
+    __syncthreads();
+    if (count >= repeats) break;
+  }
+  if (tid == 0) verdict[row] = count >= repeats;
+}
+
+size_t loop_guard_smem(int token_bytes) { return (size_t)(LG_CH + 2 * LG_MAXW) * token_bytes; }
+
+cudaError_t launch_loop_guard(const void* tokens, int token_bytes, int rows, int64_t stride, const int32_t* lengths,
+                              int window, int repeats, uint8_t* verdict, cudaStream_t stream) {
+  const size_t smem = loop_guard_smem(token_bytes);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int configured[64][2] = {};
+  const bool fresh = dev >= 0 && dev < 64 && !configured[dev][token_bytes == 8];
+  if (token_bytes == 4) {
+    if (fresh) {
+      cudaFuncSetAttribute(loop_guard_kernel<int32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      configured[dev][0] = 1;
+    }
+    loop_guard_kernel<int32_t><<<rows, LG_NT, smem, stream>>>(reinterpret_cast<const int32_t*>(tokens), stride,
+                                                                lengths, window, repeats, verdict);
+  } else {
+    if (fresh) {
+      cudaFuncSetAttribute(loop_guard_kernel<int64_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      configured[dev][1] = 1;
+    }
+    loop_guard_kernel<int64_t><<<rows, LG_NT, smem, stream>>>(reinterpret_cast<const int64_t*>(tokens), stride,
+                                                                lengths, window, repeats, verdict);
+  }
+  return cudaGetLastError();
+}
+
+int loop_guard_max_window() { return LG_MAXW; }
+
+}  // namespace sv

@@ -1,0 +1,240 @@
+"""Tensor-level wrappers of the C ABI (torch CUDA tensors in, torch CUDA tensors out).
+
+Every function enqueues on the current CUDA stream of the tensors' device and does
+not synchronise; results are device tensors.  Inputs must be CUDA tensors: there is
+no CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+_DTYPES = {torch.float32: L.F32, torch.float16: L.F16, torch.bfloat16: L.BF16}
+
+
+def _need_cuda(t, name):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (the B200 sampling kernels have no CPU path)")
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _rows(logits):
+    _need_cuda(logits, "logits")
+    if logits.dim() == 1:
+        logits = logits.unsqueeze(0)
+    if logits.dim() != 2:
+        raise ValueError("logits must be [rows, vocab]")
+    if logits.dtype not in _DTYPES:
+        raise ValueError(f"unsupported logits dtype {logits.dtype}")
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
+    return logits
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _history(rows, vocab, history=None, history_len=None, seen=None, seen_bits=None):
+    """(pointer, kind, row stride, len pointer, cols, keep-alive) for one history form."""
+    if sum(x is not None for x in (history, seen, seen_bits)) > 1:
+        raise ValueError("pass at most one of history, seen, seen_bits")
+    if history is not None:
+        _need_cuda(history, "history")
+        h = history if history.dim() == 2 else history.unsqueeze(0)
+        if h.dtype not in (torch.int32, torch.int64):
+            raise ValueError("history ids must be int32 or int64")
+        if h.stride(-1) != 1:
+            h = h.contiguous()
+        kind = L.HIST_IDS32 if h.dtype == torch.int32 else L.HIST_IDS64
+        stride = h.stride(0) if h.shape[0] > 1 else 0
+        lens = None
+        if history_len is not None:
+            lens = history_len.to(device=h.device, dtype=torch.int32).contiguous()
+        return h.data_ptr(), kind, stride, _ptr(lens), h.shape[1], (h, lens)
+    if seen is not None:
+        _need_cuda(seen, "seen")
+        s = seen if seen.dim() == 2 else seen.unsqueeze(0)
+        if s.dtype not in (torch.bool, torch.uint8):
+            raise ValueError("seen must be bool or uint8")
+        if s.stride(-1) != 1:
+            s = s.contiguous()
+        stride = s.stride(0) if s.shape[0] > 1 else 0
+        return s.data_ptr(), L.HIST_MASK8, stride, None, 0, (s,)
+    if seen_bits is not None:
+        _need_cuda(seen_bits, "seen_bits")
+        b = seen_bits if seen_bits.dim() == 2 else seen_bits.unsqueeze(0)
+        if b.dtype != torch.int32 or b.stride(-1) != 1:
+            raise ValueError("seen_bits must be a contiguous int32 bitmap [rows, ceil(vocab/32)]")
+        stride = b.stride(0) if b.shape[0] > 1 else 0
+        return b.data_ptr(), L.HIST_BITS32, stride, None, 0, (b,)
+    return None, L.HIST_NONE, 0, None, 0, ()
+
+
+def seen_bitmap(rows, vocab, device):
+    """An all-clear packed seen bitmap [rows, ceil(vocab/32)] (int32 storage)."""
+    return torch.zeros((rows, (vocab + 31) // 32), dtype=torch.int32, device=device)
+
+
+def sample_step(logits, uniforms, *, history=None, history_len=None, seen=None, seen_bits=None,
+                temperature=1.5, top_p=0.9, top_k=50, keep=1, repetition_penalty=3.1, out_capacity=0,
+                dense=None, update_seen_bits=None, force_general=False, out=None):
+    """Fused penalty + temperature + top-k + top-p + softmax + draw for each row.
+
+    Mirrors runtime_shared.py:200-202 per row (see include/starvector_sampling.h).
+    Returns a dict: token int64 [R], count int32 [R], status int32 [R], and when
+    requested idx/prob/score [R, out_capacity] (kept tokens in index order) and
+    dense [R, V] ('scores' = the _warp output, 'probs' = its softmax).
+    """
+    x = _rows(logits)
+    R, V = x.shape
+    dev = x.device
+    _need_cuda(uniforms, "uniforms")
+    u = uniforms.reshape(-1)
+    if u.dtype != torch.float32 or not u.is_contiguous() or u.numel() < R:
+        raise ValueError("uniforms must be a contiguous float32 tensor with one value per row")
+    hp, hk, hs, hl, hc, _keep = _history(R, V, history, history_len, seen, seen_bits)
+    o = out if out is not None else {}  # filled in place: callers may preallocate
+    if "token" not in o:
+        o["token"] = torch.empty(R, dtype=torch.int64, device=dev)
+    if "count" not in o:
+        o["count"] = torch.empty(R, dtype=torch.int32, device=dev)
+    if "status" not in o:
+        o["status"] = torch.empty(R, dtype=torch.int32, device=dev)
+    if out_capacity and "idx" not in o:
+        o["idx"] = torch.full((R, out_capacity), -1, dtype=torch.int32, device=dev)
+        o["prob"] = torch.zeros((R, out_capacity), dtype=torch.float32, device=dev)
+        o["score"] = torch.zeros((R, out_capacity), dtype=torch.float32, device=dev)
+    mode = {None: L.DENSE_NONE, "scores": L.DENSE_SCORES, "probs": L.DENSE_PROBS}[dense]
+    if mode != L.DENSE_NONE and "dense" not in o:
+        o["dense"] = torch.empty((R, V), dtype=torch.float32, device=dev)
+    upd = update_seen_bits
+    if upd is not None:
+        _need_cuda(upd, "update_seen_bits")
+    rc = L.lib().sv_sample_step(
+        x.data_ptr(), _DTYPES[x.dtype], R, V, x.stride(0) if R > 1 else 0, hp, hk, hs, hl, hc, u.data_ptr(),
+        float(temperature), float(top_p), int(top_k), int(keep), float(repetition_penalty),
+        o["token"].data_ptr(), o["count"].data_ptr(), _ptr(o.get("idx")), _ptr(o.get("prob")), _ptr(o.get("score")),
+        int(out_capacity), _ptr(o.get("dense")), mode, V, o["status"].data_ptr(),
+        _ptr(upd), 0 if upd is None else (upd.stride(0) if upd.dim() == 2 else upd.shape[-1]),
+        L.FLAG_FORCE_GENERAL if force_general else 0, _stream(dev))
+    L.check(rc, "sv_sample_step")
+    return o
+
+
+_WORKSPACES = {}
+
+
+def beam_workspace(beams, vocab, device):
+    """A zero-filled workspace for sv_beam_step, cached per (device, stream, shape).
+
+    Calls that overlap on the GPU must not share a workspace; the cache keys on the
+    current stream for that reason."""
+    device = torch.device(device)
+    key = (device.index, _stream(device), beams, vocab)
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        nbytes = L.lib().sv_beam_workspace_bytes(int(beams), int(vocab))
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def beam_step(logits, running_scores, uniforms, *, history=None, history_len=None, seen=None, seen_bits=None,
+              temperature=1.5, top_p=0.9, top_k=50, keep=2, repetition_penalty=3.1, num_picks=None,
+              out_capacity=0, dense_logprob=False, force_general=False, workspace=None, out=None):
+    """One beam-sampling step (runtime_shared.py:230-237); see include/starvector_sampling.h.
+
+    Returns a dict: picks int64 [P] (flattened beam*V + token), scores float [P],
+    n int32 [1] (valid picks), status int32 [1]; optionally per-beam kept lists
+    kept_count/kept_idx/kept_logprob/kept_prob and dense logprob [B, V].
+    """
+    x = _rows(logits)
+    B, V = x.shape
+    dev = x.device
+    P = 2 * B if num_picks is None else int(num_picks)
+    rs = running_scores.reshape(-1)
+    _need_cuda(rs, "running_scores")
+    if rs.dtype != torch.float32 or not rs.is_contiguous() or rs.numel() != B:
+        raise ValueError("running_scores must be a contiguous float32 tensor [beams]")
+    u = uniforms.reshape(-1)
+    _need_cuda(u, "uniforms")
+    if u.dtype != torch.float32 or not u.is_contiguous() or u.numel() < P:
+        raise ValueError("uniforms must be a contiguous float32 tensor with num_picks values")
+    hp, hk, hs, hl, hc, _keep = _history(B, V, history, history_len, seen, seen_bits)
+    o = out if out is not None else {}  # filled in place: callers may preallocate
+    o.setdefault("picks", torch.full((P,), -1, dtype=torch.int64, device=dev))
+    o.setdefault("scores", torch.zeros(P, dtype=torch.float32, device=dev))
+    o.setdefault("n", torch.zeros(1, dtype=torch.int32, device=dev))
+    o.setdefault("status", torch.zeros(1, dtype=torch.int32, device=dev))
+    if out_capacity:
+        o.setdefault("kept_count", torch.zeros(B, dtype=torch.int32, device=dev))
+        o.setdefault("kept_idx", torch.full((B, out_capacity), -1, dtype=torch.int32, device=dev))
+        o.setdefault("kept_logprob", torch.zeros((B, out_capacity), dtype=torch.float32, device=dev))
+        o.setdefault("kept_prob", torch.zeros((B, out_capacity), dtype=torch.float32, device=dev))
+    if dense_logprob:
+        o.setdefault("dense_logprob", torch.empty((B, V), dtype=torch.float32, device=dev))
+    ws = workspace if workspace is not None else beam_workspace(B, V, dev)
+    rc = L.lib().sv_beam_step(
+        x.data_ptr(), _DTYPES[x.dtype], B, V, x.stride(0) if B > 1 else 0, hp, hk, hs, hl, hc, rs.data_ptr(),
+        u.data_ptr(), P, float(temperature), float(top_p), int(top_k), int(keep), float(repetition_penalty),
+        o["picks"].data_ptr(), o["scores"].data_ptr(), o["n"].data_ptr(), o["status"].data_ptr(),
+        _ptr(o.get("kept_count")), _ptr(o.get("kept_idx")), _ptr(o.get("kept_logprob")), _ptr(o.get("kept_prob")),
+        int(out_capacity), _ptr(o.get("dense_logprob")), V, ws.data_ptr(), ws.numel(),
+        L.FLAG_FORCE_GENERAL if force_general else 0, _stream(dev))
+    L.check(rc, "sv_beam_step")
+    return o
+
+
+def loop_guard(tokens, lengths=None, window=64, repeats=3, out=None):
+    """Loop-guard verdicts (bool [R]) for token rows [R, L] (runtime_shared.py:156-167)."""
+    _need_cuda(tokens, "tokens")
+    t = tokens if tokens.dim() == 2 else tokens.unsqueeze(0)
+    if t.dtype not in (torch.int32, torch.int64):
+        raise ValueError("tokens must be int32 or int64")
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    R, Lmax = t.shape
+    if lengths is None:
+        lengths = torch.full((R,), Lmax, dtype=torch.int32, device=t.device)
+    ln = lengths.to(device=t.device, dtype=torch.int32).contiguous()
+    v = out if out is not None else torch.empty(R, dtype=torch.uint8, device=t.device)
+    rc = L.lib().sv_loop_guard(t.data_ptr(), t.element_size(), R, t.stride(0) if R > 1 else 0, ln.data_ptr(),
+                               int(window), int(repeats), v.data_ptr(), _stream(t.device))
+    L.check(rc, "sv_loop_guard")
+    return v.bool() if out is None else v
+
+
+def penalize(logits, seen=None, seen_bits=None, repetition_penalty=3.1):
+    """The reference's _penalize (runtime_shared.py:170-173) as float32 [R, V]."""
+    x = _rows(logits)
+    R, V = x.shape
+    hp, hk, hs, _, _, _keep = _history(R, V, None, None, seen, seen_bits)
+    if hk == L.HIST_NONE:
+        raise ValueError("penalize needs seen or seen_bits")
+    out = torch.empty((R, V), dtype=torch.float32, device=x.device)
+    rc = L.lib().sv_penalize(x.data_ptr(), _DTYPES[x.dtype], R, V, x.stride(0) if R > 1 else 0, hp, hk, hs,
+                             float(repetition_penalty), out.data_ptr(), V, _stream(x.device))
+    L.check(rc, "sv_penalize")
+    return out
+
+
+def seen_update(seen_bits, tokens, vocab):
+    """seen[r, tokens[r]] = True on a packed bitmap."""
+    t = tokens.reshape(-1).to(torch.int64).contiguous()
+    rc = L.lib().sv_seen_update(seen_bits.data_ptr(), seen_bits.shape[0], seen_bits.stride(0), t.data_ptr(),
+                                int(vocab), _stream(seen_bits.device))
+    L.check(rc, "sv_seen_update")
+
+
+def seen_reorder(src, dst, parents, tokens, vocab):
+    """dst[b] = src[parents[b]] with bit tokens[b] set (runtime_shared.py:258-259)."""
+    p = parents.reshape(-1).to(torch.int64).contiguous()
+    t = None if tokens is None else tokens.reshape(-1).to(torch.int64).contiguous()
+    rc = L.lib().sv_seen_reorder(src.data_ptr(), dst.data_ptr(), src.shape[0], int(vocab), src.stride(0),
+                                 p.data_ptr(), _ptr(t), _stream(src.device))
+    L.check(rc, "sv_seen_reorder")

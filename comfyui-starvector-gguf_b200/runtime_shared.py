@@ -1,0 +1,265 @@
+"""Drop-in for the sampling part of ComfyUI-StarVector-GGUF's runtime_shared.py.
+
+Same names, arguments, return values and errors as the reference's sampling API
+(runtime_shared.py:147-342): the constants, `_repeating`, `_penalize`, `_warp`,
+`_ends`, `_sample`, `_beam_sample` and `generate_tokens`.  The decoder protocol is
+unchanged (`context`, `embed(ids)`, `prefill(embeddings, rows, capacity)` returning
+a decoding object with `step(tokens)` / `reorder(parents)` plus the first logits).
+
+What changes is where the per-token sampling step runs: one fused sm_100a kernel
+per step (penalty from an on-device seen bitmap, temperature, top-k, top-p,
+softmax, draw, seen update), the beam step in one launch, and the loop guard on a
+device-resident token history.  Draws come from uniforms generated on the device
+from the same seed (`torch.manual_seed(seed)` inside `fork_rng`, as the reference);
+the draw rule is an inverse CDF over the kept tokens, so the sampled distribution
+equals torch.multinomial's while individual samples differ from the reference's
+for the same seed.  Logits must live on a CUDA device.
+"""
+from __future__ import annotations
+
+import logging
+from time import perf_counter
+
+import torch
+
+from . import _lib as L
+from . import ops
+
+# Transformers' sampling settings of the StarVector quickstart (runtime_shared.py:147-153).
+TOP_K = 50
+REPETITION_PENALTY = 3.1
+LENGTH_PENALTY = -1.0
+LOOP_WINDOW = 64
+LOOP_REPEATS = 3
+
+logger = logging.getLogger(__name__)
+
+
+def _raise_status(status: int) -> None:
+    raise RuntimeError(f"probability tensor contains either `inf`, `nan` or element < 0 "
+                       f"({L.error_string(status)})")
+
+
+def _repeating(tokens, device=None):
+    """True when the last LOOP_WINDOW tokens occur LOOP_REPEATS times (runtime_shared.py:156-167).
+
+    `tokens` is a host list (as in the reference) or a CUDA int tensor [L]."""
+    if isinstance(tokens, torch.Tensor):
+        t = tokens.reshape(1, -1)
+    else:
+        if len(tokens) < LOOP_WINDOW * LOOP_REPEATS:
+            return False
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        t = torch.tensor([list(tokens)], dtype=torch.int32, device=dev)
+    if t.shape[1] < LOOP_WINDOW * LOOP_REPEATS:
+        return False
+    return bool(ops.loop_guard(t, window=LOOP_WINDOW, repeats=LOOP_REPEATS)[0])
+
+
+def _penalize(scores, seen):
+    """Transformers' RepetitionPenaltyLogitsProcessor over the generated tokens (:170-173)."""
+    return ops.penalize(scores, seen=seen, repetition_penalty=REPETITION_PENALTY).reshape(scores.shape)
+
+
+def _warp(scores, temperature, top_p, keep):
+    """Transformers' temperature, top-k and top-p warpers, in that order (:176-187)."""
+    x = scores.reshape(-1, scores.shape[-1])
+    u = torch.zeros(x.shape[0], dtype=torch.float32, device=x.device)
+    o = ops.sample_step(x, u, temperature=temperature, top_p=top_p, top_k=TOP_K, keep=keep,
+                        repetition_penalty=REPETITION_PENALTY, dense="scores")
+    status = o["status"].max().item()
+    if status:
+        _raise_status(int(status))
+    return o["dense"].reshape(scores.shape)
+
+
+def _ends(tokens, stop_ids, eos_id):
+    return tokens[-1] == eos_id or tokens[-len(stop_ids):] == stop_ids
+
+
+class _TokenHistory:
+    """Device copy of each row's generated tokens, for the loop guard."""
+
+    def __init__(self, rows, capacity, device):
+        self.ids = torch.zeros((rows, max(capacity, 1)), dtype=torch.int32, device=device)
+        self.spare = torch.empty_like(self.ids)
+        self.length = 0
+
+    def append(self, tokens):
+        self.ids[:, self.length].copy_(tokens)
+        self.length += 1
+
+    def reorder(self, parents):
+        torch.index_select(self.ids, 0, parents, out=self.spare)
+        self.ids, self.spare = self.spare, self.ids
+
+    def repeating(self, row=0):
+        if self.length < LOOP_WINDOW * LOOP_REPEATS:
+            return False
+        lengths = torch.full((1,), self.length, dtype=torch.int32, device=self.ids.device)
+        return bool(ops.loop_guard(self.ids[row:row + 1], lengths, LOOP_WINDOW, LOOP_REPEATS)[0])
+
+
+def _sample(decoder, embeddings, max_new_tokens, temperature, top_p, stop_ids, eos_id, loop_guard, on_step,
+            uniforms=None):
+    """Transformers' multinomial sampling of one sequence (runtime_shared.py:194-211)."""
+    decoding, logits = decoder.prefill(embeddings, 1, embeddings.shape[1] + max_new_tokens)
+    device, vocab = logits.device, logits.shape[-1]
+    if uniforms is None:
+        uniforms = torch.rand((max_new_tokens, 1), dtype=torch.float32, device=device)
+    seen = ops.seen_bitmap(1, vocab, device)
+    history = _TokenHistory(1, max_new_tokens, device)
+    out = {}
+    tokens = []
+    for step in range(max_new_tokens):
+        out = ops.sample_step(logits.reshape(1, vocab), uniforms[step], seen_bits=seen, temperature=temperature,
+                              top_p=top_p, top_k=TOP_K, keep=1, repetition_penalty=REPETITION_PENALTY,
+                              update_seen_bits=seen, out=out)
+        token = out["token"]
+        history.append(token)
+        value = int(token)
+        if value < 0:
+            _raise_status(int(out["status"][0]))
+        tokens.append(value)
+        on_step(step + 1)
+        if _ends(tokens, stop_ids, eos_id):
+            return tokens, 'stop'
+        if loop_guard and step % 16 == 15 and history.repeating():
+            return tokens, 'repetition'
+        if step + 1 < max_new_tokens:
+            logits = decoding.step(token)
+    return tokens, 'token_limit'
+
+
+def _beam_sample(decoder, embeddings, max_new_tokens, temperature, top_p, beams, stop_ids, eos_id, loop_guard,
+                 on_step, uniforms=None):
+    """Transformers' beam sampling with early_stopping=True for one prompt (runtime_shared.py:214-265).
+
+    Each step samples 2 * beams continuations without replacement from all beams.
+    Only the first `beams` samples may finish; the best unfinished samples continue.
+    Finished scores use the length penalty.
+    """
+    keep = 2 * beams
+    decoding, logits = decoder.prefill(embeddings, beams, embeddings.shape[1] + max_new_tokens)
+    device, vocab = logits.device, logits.shape[-1]
+    if uniforms is None:
+        uniforms = torch.rand((max_new_tokens, keep), dtype=torch.float32, device=device)
+    running = [[] for _ in range(beams)]
+    running_scores = [0.] + [-1e9] * (beams - 1)
+    seen, seen_next = ops.seen_bitmap(beams, vocab, device), ops.seen_bitmap(beams, vocab, device)
+    finished = []
+    improvable = True
+    host = torch.empty(2 * keep + 2, dtype=torch.float64, pin_memory=True)
+    out = {}
+    for step in range(max_new_tokens):
+        scores_t = torch.tensor(running_scores, dtype=torch.float32, device=device)
+        out = ops.beam_step(logits.reshape(-1, vocab), scores_t, uniforms[step], seen_bits=seen,
+                            temperature=temperature, top_p=top_p, top_k=TOP_K, keep=2,
+                            repetition_penalty=REPETITION_PENALTY, num_picks=keep, out=out)
+        # One device->host transfer for picks, picked scores, count and status.
+        packed = torch.cat((out["picks"].double(), out["scores"].double(), out["n"].double(),
+                            out["status"].double()))
+        host.copy_(packed, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        vals = host.tolist()
+        n, status = int(vals[2 * keep]), int(vals[2 * keep + 1])
+        if status:
+            _raise_status(status)
+        picks = [int(v) for v in vals[:n]]
+        picked = vals[keep:keep + n]  # float32 scores, exact as doubles (:236)
+        parents, tokens = zip(*(divmod(pick, vocab) for pick in picks))
+        candidates = [running[parent] + [token] for parent, token in zip(parents, tokens)]
+        last = step + 1 == max_new_tokens
+        hits = [last or _ends(candidate, stop_ids, eos_id) for candidate in candidates]
+        if improvable and len(finished) < beams:
+            finished += [(picked[j] / (step + 1) ** LENGTH_PENALTY, candidates[j])
+                         for j in range(min(beams, len(picked))) if hits[j]]
+            finished = sorted(finished, key=lambda item: item[0], reverse=True)[:beams]
+        live = [score - 1e9 * hit for score, hit in zip(picked, hits)]
+        order = sorted(range(len(picked)), key=live.__getitem__, reverse=True)[:beams]
+        running_scores = [live[j] for j in order] + [-1e9] * (beams - len(order))
+        order += [order[0]] * (beams - len(order))
+        running = [candidates[j] for j in order]
+        on_step(step + 1)
+        worst = min(score for score, _ in finished) if len(finished) == beams else -1e9
+        improvable = improvable and running_scores[0] / (step + 1) ** LENGTH_PENALTY > worst
+        if not improvable or len(finished) == beams or all(hits):
+            break
+        if loop_guard and step % 16 == 15 and _repeating(running[0], device):
+            return (finished[0][1] if finished else running[0]), 'repetition'
+        selected = torch.tensor([parents[j] for j in order], dtype=torch.int64, device=device)
+        next_tokens = torch.tensor([tokens[j] for j in order], dtype=torch.int64, device=device)
+        ops.seen_reorder(seen, seen_next, selected, next_tokens, vocab)
+        seen, seen_next = seen_next, seen
+        decoding.reorder([parents[j] for j in order])
+        logits = decoding.step(next_tokens)
+    if not finished:
+        return running[0], 'token_limit'
+    best = finished[0][1]
+    return best, ('token_limit' if len(best) == max_new_tokens and not _ends(best, stop_ids, eos_id) else 'stop')
+
+
+def generate_tokens(decoder, tokenizer, prefix, max_new_tokens=4096, temperature=1.5, top_p=0.9, seed=0,
+                    num_beams=2, loop_guard=True, progress_callback=None):
+    """Generate SVG with StarVector's original sampling on `decoder` (runtime_shared.py:268-342).
+
+    `decoder` provides `context`, `embed(ids)` and `prefill(embeddings, rows, capacity)`,
+    which returns a decoding object with `step(tokens)` and `reorder(parents)` plus the
+    first logits.  One sequence is returned.
+    """
+    if prefix.ndim != 3 or prefix.shape[0] != 1:
+        raise ValueError("Expected one image embedding sequence [1,T,H]")
+    if max_new_tokens < 1:
+        raise ValueError("max_new_tokens must be positive")
+    if temperature <= 0:
+        raise ValueError("Sampling requires temperature > 0")
+    if not 0 < top_p <= 1:
+        raise ValueError("top_p must be in (0, 1]")
+    if not isinstance(num_beams, int) or not 1 <= num_beams <= 8:
+        raise ValueError("num_beams must be an integer between 1 and 8")
+    device = prefix.device
+    prompt_ids = tokenizer.encode("<svg")
+    stop_ids = tokenizer.encode("</svg>")
+    if not prompt_ids or not stop_ids:
+        raise ValueError("Tokenizer cannot encode SVG control tokens")
+    context = decoder.context
+    prefix_length = prefix.shape[1] + len(prompt_ids)
+    available = context - prefix_length
+    if available < 1:
+        raise ValueError(f"Generation exceeds context size {context}: "
+                         f"prefix={prefix.shape[1]}, prompt={len(prompt_ids)}")
+    requested_new_tokens = int(max_new_tokens)
+    max_new_tokens = min(requested_new_tokens, available)
+    logger.info("StarVector: context=%d, image prefix=%d, SVG prompt=%d, requested max_new_tokens=%d, "
+                "effective max_new_tokens=%d, top_k=%d, repetition_penalty=%s, loop_guard=%s", context,
+                prefix.shape[1], len(prompt_ids), requested_new_tokens, max_new_tokens, TOP_K, REPETITION_PENALTY,
+                loop_guard)
+    prompt = torch.tensor([prompt_ids], dtype=torch.long, device=device)
+    embeddings = torch.cat((prefix, decoder.embed(prompt).to(prefix.dtype)), dim=1)
+    on_step = progress_callback if progress_callback is not None else (lambda step: None)
+    cuda_devices = [device.index if device.index is not None else torch.cuda.current_device()] \
+        if device.type == "cuda" else []
+    started = perf_counter()
+    with torch.inference_mode(), torch.random.fork_rng(devices=cuda_devices):
+        torch.manual_seed(int(seed))
+        if num_beams == 1:
+            generated, reason = _sample(decoder, embeddings, max_new_tokens, float(temperature), float(top_p),
+                                        stop_ids, tokenizer.eos_token_id, loop_guard, on_step)
+        else:
+            generated, reason = _beam_sample(decoder, embeddings, max_new_tokens, float(temperature), float(top_p),
+                                             num_beams, stop_ids, tokenizer.eos_token_id, loop_guard, on_step)
+    svg = tokenizer.decode(prompt_ids + generated)
+    if not svg.startswith("<svg"):
+        raise RuntimeError("Generated text does not start with the SVG prompt")
+    elapsed = perf_counter() - started
+    has_terminator = svg.rstrip().endswith("</svg>")
+    logger.info("StarVector: decoded %d/%d tokens in %.2fs (%.2f tokens/s); beams=%d, stop=%s, "
+                "SVG terminator at end=%s", len(generated), max_new_tokens, elapsed,
+                len(generated) / max(elapsed, 1e-9), num_beams, reason, has_terminator)
+    if reason == "repetition":
+        logger.warning("StarVector: stopped after %d tokens because the model kept repeating the same output "
+                       "(loop guard)", len(generated))
+    elif not has_terminator:
+        logger.warning("StarVector: decoder stopped without a final </svg> (reason=%s, generated=%d/%d tokens); "
+                       "output tail=%r", reason, len(generated), max_new_tokens, svg[-160:])
+    return svg

@@ -1,0 +1,166 @@
+/*
+ * starvector_sampling.h -- C ABI of the B200 (sm_100a) decode-sampling kernels.
+ *
+ * A drop-in for the per-token sampling step of ComfyUI-StarVector-GGUF's native
+ * generation loop (runtime_shared.py, `generate_tokens` :268 -> `_sample` :194 /
+ * `_beam_sample` :214).  Every entry point:
+ *   - takes plain device pointers and sizes (no framework types) and a CUDA
+ *     stream (`stream`, a cudaStream_t; NULL = the legacy default stream);
+ *   - enqueues its kernels on that stream and returns without synchronising,
+ *     allocating or printing, so a call can be captured in a CUDA graph;
+ *   - returns SV_OK or a negative SV_E_* code when an argument is invalid (then
+ *     nothing is launched);
+ *   - reports data-dependent failures per row through `out_status` (SV_ST_*).
+ * Sizes: rows/beams >= 1, 1 <= vocab <= 524288, 1 <= top_k <= 128, 1 <= keep <= 128,
+ * max(top_k, keep) <= vocab.
+ */
+#ifndef STARVECTOR_SAMPLING_H
+#define STARVECTOR_SAMPLING_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes (argument errors; nothing launched). */
+#define SV_OK 0
+#define SV_E_ARG (-1)       /* null pointer or inconsistent arguments */
+#define SV_E_DTYPE (-2)     /* unknown dtype / history kind / dense mode */
+#define SV_E_SHAPE (-3)     /* rows, vocab, strides or capacities out of range */
+#define SV_E_RANGE (-4)     /* temperature <= 0, top_p outside (0, 1], top_k/keep range */
+#define SV_E_ALIGN (-5)     /* pointer not aligned to its element size */
+#define SV_E_WORKSPACE (-6) /* workspace missing or smaller than required */
+#define SV_E_CUDA (-7)      /* the CUDA launch itself failed */
+
+/* Per-row status written by the kernels (out_status). */
+#define SV_ST_OK 0
+#define SV_ST_NAN 1        /* a NaN logit (the reference's multinomial raises) */
+#define SV_ST_POSINF 2     /* +inf after penalty/temperature (softmax gives NaN) */
+#define SV_ST_ALLNEGINF 3  /* no finite logit in the row */
+#define SV_ST_HISTORY 4    /* a history id outside [0, vocab) */
+#define SV_ST_TIMEOUT 5    /* a bounded wait on an asynchronous copy ran out */
+
+/* Logit dtypes. */
+#define SV_F32 0
+#define SV_F16 1
+#define SV_BF16 2
+
+/* History kinds: the generated tokens the repetition penalty applies to. */
+#define SV_HIST_NONE 0   /* no penalty */
+#define SV_HIST_IDS32 1  /* int32 ids [rows, history_cols], valid prefix history_len[r] */
+#define SV_HIST_IDS64 2  /* int64 ids, same layout */
+#define SV_HIST_MASK8 3  /* bool/uint8 mask [rows, vocab] (the reference's `seen`) */
+#define SV_HIST_BITS32 4 /* packed bitmap uint32 [rows, ceil(vocab/32)], bit i of word i/32 */
+
+/* Dense output of sv_sample_step. */
+#define SV_DENSE_NONE 0
+#define SV_DENSE_SCORES 1 /* the warped scores: what _warp returns (-inf where masked) */
+#define SV_DENSE_PROBS 2  /* softmax of the warped scores (0 where masked) */
+
+/* Flags. */
+#define SV_FLAG_FORCE_GENERAL 1 /* take the general (tie-group) path for every row */
+
+/*
+ * One sample-mode step for `rows` independent sequences.
+ * Replaces, per row, runtime_shared.py:200-202:
+ *     scores = _warp(_penalize(logits.float(), seen), temperature, top_p, 1)
+ *     token  = torch.multinomial(scores.softmax(-1), 1); seen[token] = True
+ * with the draw taken from the supplied uniform: the kept tokens in ascending
+ * index order, the first whose inclusive prefix of fixed-point weights exceeds
+ * floor(u * total).
+ *   logits          [rows, row_stride] of dtype; row_stride 0 broadcasts one row
+ *                   (the prefill's expanded logits, runtime_1b.py:82)
+ *   history...      see SV_HIST_*; history_len may be NULL (= history_cols);
+ *                   lengths are clamped to [0, history_cols]
+ *   uniforms        float [rows] in [0, 1)
+ *   temperature, top_p, repetition_penalty: doubles, cast to float as torch casts
+ *                   a Python scalar; top-p is active iff top_p < 1, with
+ *                   threshold float(1 - top_p) (runtime_shared.py:182-184)
+ *   top_k, keep     runtime_shared.py:180 uses k = max(top_k, keep)
+ *   out_token       int64 [rows] (-1 on a row error)
+ *   out_count       int32 [rows] kept tokens (may be NULL)
+ *   out_idx/out_prob/out_score  [rows, out_capacity]: the first out_capacity kept
+ *                   tokens in ascending index order, their probability and warped
+ *                   score (each may be NULL)
+ *   out_dense       float [rows, dense_row_stride] per SV_DENSE_* (NULL if NONE)
+ *   out_status      int32 [rows] (may be NULL)
+ *   seen_bits_update  optional packed bitmap [rows, seen_bits_row_stride words]:
+ *                   the drawn token's bit is set (runtime_shared.py:202)
+ */
+int sv_sample_step(const void* logits, int32_t logits_dtype, int32_t rows, int32_t vocab, int64_t logits_row_stride,
+                   const void* history, int32_t history_kind, int64_t history_row_stride,
+                   const int32_t* history_len, int32_t history_cols, const float* uniforms, double temperature,
+                   double top_p, int32_t top_k, int32_t keep, double repetition_penalty, int64_t* out_token,
+                   int32_t* out_count, int32_t* out_idx, float* out_prob, float* out_score, int32_t out_capacity,
+                   float* out_dense, int32_t dense_mode, int64_t dense_row_stride, int32_t* out_status,
+                   uint32_t* seen_bits_update, int64_t seen_bits_row_stride, int32_t flags, void* stream);
+
+/* Workspace bytes sv_beam_step needs for `beams` x `vocab`.  The workspace must be
+ * zero-filled once before its first use; the kernel leaves it reusable. */
+size_t sv_beam_workspace_bytes(int32_t beams, int32_t vocab);
+
+/*
+ * One beam-sampling step (runtime_shared.py:230-237):
+ *     log_probs = _warp(_penalize(log_softmax(logits.float()), seen), T, top_p, 2)
+ *     scores    = (log_probs + running_scores[:, None]).view(1, -1)
+ *     picks     = multinomial(scores.softmax(-1), min(num_picks, count_nonzero))
+ * Draws without replacement from `uniforms[0..num_picks)`: pick j is the first
+ * remaining entry (flattened beam*vocab order) whose inclusive prefix weight
+ * exceeds floor(u_j * remaining total).  The host keeps the divmod, finishing,
+ * length penalty and ordering logic (runtime_shared.py:237-260).
+ *   running_scores  float [beams]; uniforms float [num_picks]; num_picks <= 64
+ *   out_picks       int64 [num_picks] flattened indices b*vocab + token
+ *   out_pick_scores float [num_picks] = scores at the picks (:236)
+ *   out_num_picks   int32 [1]; out_status int32 [1]
+ *   out_kept_*      optional per-beam kept tokens [beams, out_capacity] (index
+ *                   order): ids, warped log-probs, probabilities over beams*vocab
+ *   out_dense_logprob optional float [beams, dense_row_stride]: log_probs as above
+ */
+int sv_beam_step(const void* logits, int32_t logits_dtype, int32_t beams, int32_t vocab, int64_t logits_row_stride,
+                 const void* history, int32_t history_kind, int64_t history_row_stride, const int32_t* history_len,
+                 int32_t history_cols, const float* running_scores, const float* uniforms, int32_t num_picks,
+                 double temperature, double top_p, int32_t top_k, int32_t keep, double repetition_penalty,
+                 int64_t* out_picks, float* out_pick_scores, int32_t* out_num_picks, int32_t* out_status,
+                 int32_t* out_kept_count, int32_t* out_kept_idx, float* out_kept_logprob, float* out_kept_prob,
+                 int32_t out_capacity, float* out_dense_logprob, int64_t dense_row_stride, void* workspace,
+                 size_t workspace_bytes, int32_t flags, void* stream);
+
+/*
+ * Loop guard for `rows` token histories (runtime_shared.py:156-167, `_repeating`):
+ * verdict[r] = 1 iff lengths[r] >= window*repeats and the last `window` tokens of
+ * row r occur at least `repeats` times.  tokens int32 or int64 (token_bytes 4/8)
+ * [rows, row_stride]; 1 <= window <= 1024.  lengths[r] is clamped to row_stride
+ * when row_stride > 0 (with row_stride 0 the caller guarantees the length).
+ */
+int sv_loop_guard(const void* tokens, int32_t token_bytes, int32_t rows, int64_t row_stride, const int32_t* lengths,
+                  int32_t window, int32_t repeats, uint8_t* out_verdict, void* stream);
+
+/* The reference's _penalize on its own (runtime_shared.py:170-173): out =
+ * seen ? (x < 0 ? x*p : x/p) : x as float [rows, out_row_stride]; history kinds
+ * SV_HIST_MASK8 or SV_HIST_BITS32. */
+int sv_penalize(const void* logits, int32_t logits_dtype, int32_t rows, int32_t vocab, int64_t logits_row_stride,
+                const void* history, int32_t history_kind, int64_t history_row_stride, double repetition_penalty,
+                float* out, int64_t out_row_stride, void* stream);
+
+/* seen[r, tokens[r]] = 1 on a packed bitmap (runtime_shared.py:202). */
+int sv_seen_update(uint32_t* seen_bits, int32_t rows, int64_t row_stride_words, const int64_t* tokens,
+                   int32_t vocab, void* stream);
+
+/* dst[b] = src[parents[b]] with bit tokens[b] set (runtime_shared.py:258-259);
+ * tokens may be NULL.  src and dst must not overlap. */
+int sv_seen_reorder(const uint32_t* src, uint32_t* dst, int32_t beams, int32_t vocab, int64_t row_stride_words,
+                    const int64_t* parents, const int64_t* tokens, void* stream);
+
+/* Text of a return or status code. */
+const char* sv_error_string(int32_t code);
+
+/* ABI version of this library. */
+int32_t sv_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STARVECTOR_SAMPLING_H */

@@ -199,7 +199,7 @@ static void work_free(work_t *w)
  * runtime_shared.py:170-187.  On return s holds the warped scores (-inf where
  * masked).  *pmax receives the row maximum M (the maximum of the warped scores).
  *   pen: seen ? (s < 0 ? s*rp : s/rp) : s            (:172-173)
- *   temperature: s / T                                (:178-179; x/1 == x)
+ *   temperature: s / T, then -0 -> +0                 (:178-179; x/1 == x)
  *   top-k: thr = kk-th largest, s < thr -> -inf       (:180-181)
  *   top-p: ascending sort, softmax, cumsum <= 1-top_p removed,
  *          last `keep` never removed, scatter back     (:182-186)
@@ -210,7 +210,9 @@ static int warp_row(work_t *w, float *s, int64_t V, const uint8_t *seen, float T
     for (int64_t i = 0; i < V; i++) {
         float v = s[i];
         if (seen && seen[i]) v = (v < 0.0f) ? v * rp : v / rp;
-        v = v / T;
+        /* Temperature, then -0 -> +0: torch compares -0 == +0, and the canonical
+         * zero keeps the ordered-key sort consistent with float comparisons. */
+        v = v / T + 0.0f;
         if (v != v) return ORC_ERR_NAN;
         if (v == INFINITY) return ORC_ERR_POSINF;
         s[i] = v;
@@ -283,6 +285,10 @@ static int sample_row(work_t *w, const float *x, int64_t V, const uint8_t *seen,
     int st = warp_row(w, s, V, seen, T, rp, pthr, kk, keep, &M);
     if (st != ORC_OK) {
         *token = -1; *count = 0;
+        for (int64_t i = 0; i < V; i++) {
+            if (dscores) dscores[i] = -INFINITY;
+            if (dprobs) dprobs[i] = 0.0f;
+        }
         return st;
     }
     uint64_t total;

@@ -1,0 +1,94 @@
+"""The C-ABI library without a GPU: it loads, exports every function that
+include/*.h declares, and rejects invalid arguments with the documented codes
+before touching the device (no kernel launch, no CUDA call)."""
+import ctypes as C
+import glob
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        names |= set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(sv_\w+)\s*\(", text, re.M))
+    return names
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for n in ("sv_sample_step", "sv_beam_step", "sv_beam_workspace_bytes", "sv_loop_guard", "sv_penalize",
+              "sv_seen_update", "sv_seen_reorder", "sv_error_string", "sv_abi_version"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(sv):
+    lib = sv._lib.lib()
+    out = subprocess.run(["nm", "-D", "--defined-only", sv._lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\sT\s(sv_\w+)", out))
+    for name in declared_functions():
+        assert name in exported, name
+        assert getattr(lib, name) is not None
+
+
+def test_abi_version_and_error_strings(sv):
+    lib = sv._lib.lib()
+    assert lib.sv_abi_version() == 1
+    assert sv._lib.error_string(-4).startswith("temperature")
+    assert sv._lib.error_string(1) == "NaN logit in row"
+
+
+def test_workspace_size(sv):
+    lib = sv._lib.lib()
+    assert lib.sv_beam_workspace_bytes(2, 49152) > 2 * 49152 * 16
+    assert lib.sv_beam_workspace_bytes(0, 10) == 0
+
+
+def _sample(lib, **kw):
+    args = dict(logits=8, dtype=0, rows=1, vocab=100, stride=100, hist=None, hkind=0, hstride=0, hlen=None, hcols=0,
+                u=8, T=1.5, p=0.9, k=50, keep=1, rp=3.1, tok=8, cnt=None, idx=None, prob=None, score=None, cap=0,
+                dense=None, dmode=0, dstride=0, st=None, bits=None, bstride=0, flags=0, stream=None)
+    args.update(kw)
+    return lib.sv_sample_step(*args.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(logits=None), -1), (dict(dtype=7), -2), (dict(rows=0), -3), (dict(vocab=600000), -3),
+    (dict(stride=50), -3), (dict(T=0.0), -4), (dict(T=-1.0), -4), (dict(p=0.0), -4), (dict(p=1.1), -4),
+    (dict(k=0), -4), (dict(k=129), -4), (dict(keep=0), -4), (dict(vocab=40, stride=40), -4),
+    (dict(logits=2), -5), (dict(u=None), -1), (dict(tok=None), -1), (dict(dmode=1), -1), (dict(hkind=9), -2),
+    (dict(hkind=1, hist=None), -1), (dict(rp=0.0), -4),
+])
+def test_sample_step_rejects_invalid_arguments(sv, kw, code):
+    assert _sample(sv._lib.lib(), **kw) == code
+
+
+def test_beam_step_rejects_bad_workspace_and_counts(sv):
+    lib = sv._lib.lib()
+    base = [8, 0, 2, 100, 100, None, 0, 0, None, 0, 8, 8, 4, 1.5, 0.9, 50, 2, 3.1, 8, 8, 8, 8,
+            None, None, None, None, 0, None, 0, 16, 0, 0, None]
+    a = list(base)
+    a[29] = 16
+    a[30] = 10  # workspace too small
+    assert lib.sv_beam_step(*a) == -6
+    a = list(base)
+    a[2] = 33   # beams > 32
+    a[30] = 1 << 30
+    assert lib.sv_beam_step(*a) == -3
+    a = list(base)
+    a[12] = 65  # num_picks > 64
+    a[30] = 1 << 30
+    assert lib.sv_beam_step(*a) == -3
+
+
+def test_loop_guard_rejects_invalid_arguments(sv):
+    lib = sv._lib.lib()
+    assert lib.sv_loop_guard(None, 4, 1, 10, 8, 64, 3, 8, None) == -1
+    assert lib.sv_loop_guard(8, 2, 1, 10, 8, 64, 3, 8, None) == -2
+    assert lib.sv_loop_guard(8, 4, 1, 10, 8, 2000, 3, 8, None) == -4
+    assert lib.sv_loop_guard(8, 4, 0, 10, 8, 64, 3, 8, None) == -3
