@@ -283,6 +283,7 @@ const char* sv_error_string(int32_t code) {
     case SV_E_ALIGN: return "pointer not aligned to its element size";
     case SV_E_WORKSPACE: return "workspace missing or too small";
     case SV_E_CUDA: return "CUDA launch failed";
+    case SV_E_NOALLOC_LIMIT: return "beams x vocab exceed the fixed scratch of sv_beam_step_noalloc (8 MiB)";
     case SV_ST_NAN: return "NaN logit in row";
     case SV_ST_POSINF: return "+inf score in row";
     case SV_ST_ALLNEGINF: return "no finite logit in row";

@@ -33,6 +33,7 @@ extern "C" {
 #define SV_E_ALIGN (-5)     /* pointer not aligned to its element size */
 #define SV_E_WORKSPACE (-6) /* workspace missing or smaller than required */
 #define SV_E_CUDA (-7)      /* the CUDA launch itself failed */
+#define SV_E_NOALLOC_LIMIT (-8) /* sv_beam_step_noalloc: beams x vocab beyond its fixed scratch */
 
 /* Per-row status written by the kernels (out_status). */
 #define SV_ST_OK 0
@@ -126,6 +127,30 @@ int sv_beam_step(const void* logits, int32_t logits_dtype, int32_t beams, int32_
                  int32_t* out_kept_count, int32_t* out_kept_idx, float* out_kept_logprob, float* out_kept_prob,
                  int32_t out_capacity, float* out_dense_logprob, int64_t dense_row_stride, void* workspace,
                  size_t workspace_bytes, int32_t flags, void* stream);
+
+/*
+ * sv_beam_step_noalloc: sv_beam_step for callers that cannot allocate device
+ * memory.  No counterpart in the reference (its beam step allocates through torch).
+ * A host application that owns the GPU's memory and forbids plugins to allocate, or
+ * a loop that must not allocate during a step, cannot provide sv_beam_step's
+ * workspace; this variant uses a fixed 8 MiB array that the library declares in
+ * device memory instead (held by every GPU that loads the library until the
+ * process exits).  Arguments and results are sv_beam_step's, without the workspace.
+ * Limit: sv_beam_workspace_bytes(beams, vocab) <= 8 MiB, i.e. beams * vocab <=
+ * 524271 (8 beams up to vocab 65533); larger calls return SV_E_NOALLOC_LIMIT.
+ * The first call on a device looks up the array's device address (make it before
+ * any stream capture).  Each call clears the array's header on `stream`.  All calls
+ * share the array: calls that overlap on the GPU race.
+ */
+int sv_beam_step_noalloc(const void* logits, int32_t logits_dtype, int32_t beams, int32_t vocab,
+                         int64_t logits_row_stride, const void* history, int32_t history_kind,
+                         int64_t history_row_stride, const int32_t* history_len, int32_t history_cols,
+                         const float* running_scores, const float* uniforms, int32_t num_picks, double temperature,
+                         double top_p, int32_t top_k, int32_t keep, double repetition_penalty, int64_t* out_picks,
+                         float* out_pick_scores, int32_t* out_num_picks, int32_t* out_status,
+                         int32_t* out_kept_count, int32_t* out_kept_idx, float* out_kept_logprob,
+                         float* out_kept_prob, int32_t out_capacity, float* out_dense_logprob,
+                         int64_t dense_row_stride, int32_t flags, void* stream);
 
 /*
  * Loop guard for `rows` token histories (runtime_shared.py:156-167, `_repeating`):
