@@ -17,6 +17,8 @@ F32, F16, BF16 = 0, 1, 2
 HIST_NONE, HIST_IDS32, HIST_IDS64, HIST_MASK8, HIST_BITS32 = range(5)
 DENSE_NONE, DENSE_SCORES, DENSE_PROBS = range(3)
 FLAG_FORCE_GENERAL = 1
+FLAG_CLUSTER = 2
+FLAG_STREAM = 4
 
 _P, _I32, _I64, _D, _SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_double, C.c_size_t
 

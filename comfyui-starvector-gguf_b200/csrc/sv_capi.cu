@@ -58,6 +58,18 @@ int split_override() {
   return v;
 }
 
+// Rows from which sv_sample_step prefers the streaming kernel; tuning override
+// SV_STREAM_MIN_ROWS, read once.
+int stream_min_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("SV_STREAM_MIN_ROWS");
+    v = e ? std::atoi(e) : 64;
+    if (v < 1) v = 1;
+  }
+  return v;
+}
+
 // Cluster split: slices of at most 48 KB; small batches spread over more SMs.
 void choose_layout(int64_t V, int es, int rows, int32_t* S_out, int32_t* slice_out, size_t* smem_out) {
   int S = 1;
@@ -163,11 +175,21 @@ int sv_sample_step(const void* logits, int32_t logits_dtype, int32_t rows, int32
   a.seen_bits = seen_bits_update;
   a.seen_bits_stride = seen_bits_row_stride;
   a.force_slow = (flags & SV_FLAG_FORCE_GENERAL) ? 1 : 0;
-  size_t smem;
-  choose_layout(vocab, esize(logits_dtype), rows, &a.S, &a.slice_len, &smem);
-  a.region_a = (uint32_t)(smem - shared_static_bytes());
-  if (smem > kSmemLimit) return SV_E_SHAPE;
-  cudaError_t e = launch_rows(a, smem, static_cast<cudaStream_t>(stream));
+  // Path: the streaming kernel for many rows when the row's seen mask fits a CTA.
+  const size_t ssmem = stream_smem_bytes(vocab);
+  bool use_stream = ssmem > 0 && rows >= stream_min_rows();
+  if (flags & SV_FLAG_CLUSTER) use_stream = false;
+  if ((flags & SV_FLAG_STREAM) && ssmem > 0) use_stream = true;
+  cudaError_t e;
+  if (use_stream) {
+    e = launch_stream(a, ssmem, static_cast<cudaStream_t>(stream));
+  } else {
+    size_t smem;
+    choose_layout(vocab, esize(logits_dtype), rows, &a.S, &a.slice_len, &smem);
+    a.region_a = (uint32_t)(smem - shared_static_bytes());
+    if (smem > kSmemLimit) return SV_E_SHAPE;
+    e = launch_rows(a, smem, static_cast<cudaStream_t>(stream));
+  }
   return e == cudaSuccess ? SV_OK : SV_E_CUDA;
 }
 

@@ -68,7 +68,12 @@ struct RowArgs {
   uint32_t region_a;  // bytes of the per-CTA union region
 };
 
+// Opt-in shared memory per CTA on sm_100 (227 KB).
+__host__ __device__ constexpr size_t smem_limit_stream() { return 232448; }
+
 size_t shared_static_bytes();
 cudaError_t launch_rows(const RowArgs& a, size_t smem_bytes, cudaStream_t stream);
+size_t stream_smem_bytes(int64_t vocab);
+cudaError_t launch_stream(const RowArgs& a, size_t smem_bytes, cudaStream_t stream);
 
 }  // namespace sv

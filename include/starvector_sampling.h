@@ -62,6 +62,8 @@ extern "C" {
 
 /* Flags. */
 #define SV_FLAG_FORCE_GENERAL 1 /* take the general (tie-group) path for every row */
+#define SV_FLAG_CLUSTER 2       /* sv_sample_step: use the cluster kernel (rows split across CTAs) */
+#define SV_FLAG_STREAM 4        /* sv_sample_step: use the streaming kernel (one CTA per row) */
 
 /*
  * One sample-mode step for `rows` independent sequences.
@@ -89,6 +91,10 @@ extern "C" {
  *   out_status      int32 [rows] (may be NULL)
  *   seen_bits_update  optional packed bitmap [rows, seen_bits_row_stride words]:
  *                   the drawn token's bit is set (runtime_shared.py:202)
+ * Two kernels implement the same arithmetic: a streaming kernel (one persistent
+ * CTA per SM walks its rows; chosen for many rows) and a cluster kernel (each row
+ * split across a thread-block cluster; chosen for few rows or vocabularies whose
+ * seen mask does not fit one CTA).  SV_FLAG_CLUSTER / SV_FLAG_STREAM force one.
  */
 int sv_sample_step(const void* logits, int32_t logits_dtype, int32_t rows, int32_t vocab, int64_t logits_row_stride,
                    const void* history, int32_t history_kind, int64_t history_row_stride,

@@ -23,8 +23,11 @@ def to_dev(a, dtype=None):
     return t.to(dtype) if dtype is not None else t
 
 
+PATHS = ["cluster", "stream"]
+
+
 def run_both(sv, x, u, *, ids=None, seen=None, form="ids32", T=1.5, p=0.9, keep=1, top_k=50, cap=None,
-             dtype=torch.float32, dense=True, force=False):
+             dtype=torch.float32, dense=True, force=False, path=None):
     R, Vv = x.shape
     cap = Vv if cap is None else cap
     xd = to_dev(x).to(dtype)
@@ -46,7 +49,7 @@ def run_both(sv, x, u, *, ids=None, seen=None, form="ids32", T=1.5, p=0.9, keep=
         else:
             kw["seen"] = to_dev(seen_np.astype(bool))
     out = sv.sample_step(xd, to_dev(u), temperature=T, top_p=p, top_k=top_k, keep=keep, out_capacity=cap,
-                         dense="probs" if dense else None, force_general=force, **kw)
+                         dense="probs" if dense else None, force_general=force, path=path, **kw)
     torch.cuda.synchronize()
     got = {k: v.cpu().numpy() for k, v in out.items()}
     ref = O.sample(xf, u, seen=seen_np, temperature=T, top_p=p, top_k=top_k, keep=keep, cap=cap, dense=dense)
@@ -66,19 +69,20 @@ def assert_same(got, ref, dense=True):
         np.testing.assert_array_equal(got["dense"], ref["probs"])
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("force", [False, True], ids=["fast", "general"])
 @pytest.mark.parametrize("name", names("proc"))
-def test_golden_cases(sv, name, force):
+def test_golden_cases(sv, name, force, path):
     d = load(name)
     x, seen = d["logits"], d["seen"]
     R = x.shape[0]
     T, p, keep = float(d["temperature"]), float(d["top_p"]), int(d["keep"])
     u = np.random.default_rng(7).random(R).astype(np.float32)
-    got, ref = run_both(sv, x, u, seen=seen, form="mask8", T=T, p=p, keep=keep, force=force)
+    got, ref = run_both(sv, x, u, seen=seen, form="mask8", T=T, p=p, keep=keep, force=force, path=path)
     assert_same(got, ref)
     # And against the reference's own output (golden): kept sets, bit-exact scores.
     out = sv.sample_step(to_dev(x), to_dev(u), seen=to_dev(seen), temperature=T, top_p=p, keep=keep,
-                         dense="scores", force_general=force)
+                         dense="scores", force_general=force, path=path)
     dense = out["dense"].cpu().numpy()
     for r in range(R):
         gi, gv = row_sparse(d, r)
@@ -89,62 +93,68 @@ def test_golden_cases(sv, name, force):
 
 
 @pytest.mark.parametrize("form", ["ids32", "ids64", "mask8", "bits32", "none"])
-def test_history_forms(sv, form):
+@pytest.mark.parametrize("path", PATHS)
+def test_history_forms(sv, form, path):
     g = np.random.default_rng(11)
     R, Vv = 6, 5000
     x = (2 * g.standard_normal((R, Vv))).astype(np.float32)
     ids = g.integers(0, Vv, (R, 700))
     u = g.random(R).astype(np.float32)
     if form == "none":
-        got, ref = run_both(sv, x, u, form="none")
+        got, ref = run_both(sv, x, u, form="none", path=path)
     else:
-        got, ref = run_both(sv, x, u, ids=ids, form=form)
+        got, ref = run_both(sv, x, u, ids=ids, form=form, path=path)
     assert_same(got, ref)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=["f32", "f16", "bf16"])
 @pytest.mark.parametrize("vocab", [128, 1000, 4099, 49152, 49157])
-def test_dtypes_and_ragged_vocab(sv, dtype, vocab):
+@pytest.mark.parametrize("path", PATHS)
+def test_dtypes_and_ragged_vocab(sv, dtype, vocab, path):
     g = np.random.default_rng(vocab)
     R = 3
     x = (2.5 * g.standard_normal((R, vocab))).astype(np.float32)
     ids = g.integers(0, vocab, (R, min(vocab, 300)))
     u = g.random(R).astype(np.float32)
-    got, ref = run_both(sv, x, u, ids=ids, dtype=dtype, cap=128)
+    got, ref = run_both(sv, x, u, ids=ids, dtype=dtype, cap=128, path=path)
     assert_same(got, ref)
 
 
 @pytest.mark.parametrize("T,p,keep", [(0.5, 0.9, 1), (1.0, 1.0, 1), (1.5, 0.5, 2), (3.0, 0.99, 1), (1.5, 0.9, 5),
                                       (0.05, 0.9, 1)])
-def test_temperature_top_p_keep(sv, T, p, keep):
+@pytest.mark.parametrize("path", PATHS)
+def test_temperature_top_p_keep(sv, T, p, keep, path):
     g = np.random.default_rng(int(T * 100) + keep)
     x = (2 * g.standard_normal((8, 8192))).astype(np.float32)
     ids = g.integers(0, 8192, (8, 500))
     u = g.random(8).astype(np.float32)
-    got, ref = run_both(sv, x, u, ids=ids, T=T, p=p, keep=keep)
+    got, ref = run_both(sv, x, u, ids=ids, T=T, p=p, keep=keep, path=path)
     assert_same(got, ref)
 
 
 @pytest.mark.parametrize("top_k", [1, 7, 64, 128])
-def test_top_k_range(sv, top_k):
+@pytest.mark.parametrize("path", PATHS)
+def test_top_k_range(sv, top_k, path):
     g = np.random.default_rng(top_k)
     x = (2 * g.standard_normal((4, 20000))).astype(np.float32)
     u = g.random(4).astype(np.float32)
-    got, ref = run_both(sv, x, u, ids=g.integers(0, 20000, (4, 100)), top_k=top_k, cap=256)
+    got, ref = run_both(sv, x, u, ids=g.integers(0, 20000, (4, 100)), top_k=top_k, cap=256, path=path)
     assert_same(got, ref)
 
 
-def test_ties_fp16_and_forced_general(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_ties_fp16_and_forced_general(sv, path):
     g = np.random.default_rng(5)
     x = np.round((3 * g.standard_normal((16, 49152))).astype(np.float16).astype(np.float32) * 2) / 2
     ids = g.integers(0, 49152, (16, 1000))
     u = g.random(16).astype(np.float32)
     for force in (False, True):
-        got, ref = run_both(sv, x.astype(np.float32), u, ids=ids, dtype=torch.float16, force=force, cap=512)
+        got, ref = run_both(sv, x.astype(np.float32), u, ids=ids, dtype=torch.float16, force=force, cap=512, path=path)
         assert_same(got, ref)
 
 
-def test_huge_tie_group_takes_general_path(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_huge_tie_group_takes_general_path(sv, path):
     """All-equal logits: top-k keeps every token (ties), top-p removes the lowest
     indices of the tie group; the candidate buffer overflows."""
     g = np.random.default_rng(6)
@@ -152,11 +162,12 @@ def test_huge_tie_group_takes_general_path(sv):
     x[1, 17] = 3.0
     x[2, :100] = 1.0
     u = np.array([0.0, 0.5, 0.999999], np.float32)
-    got, ref = run_both(sv, x, u, ids=g.integers(0, 49152, (3, 50)), cap=64)
+    got, ref = run_both(sv, x, u, ids=g.integers(0, 49152, (3, 50)), cap=64, path=path)
     assert_same(got, ref)
 
 
-def test_special_values(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_special_values(sv, path):
     g = np.random.default_rng(8)
     x = (2 * g.standard_normal((6, 3000))).astype(np.float32)
     x[0, 5] = np.nan
@@ -168,20 +179,22 @@ def test_special_values(sv):
     x[5, :] = 0.0                                         # exact zeros
     x[5, 7] = -0.0
     u = g.random(6).astype(np.float32)
-    got, ref = run_both(sv, x, u, ids=g.integers(0, 3000, (6, 40)))
+    got, ref = run_both(sv, x, u, ids=g.integers(0, 3000, (6, 40)), path=path)
     np.testing.assert_array_equal(got["status"], [1, 2, 3, 0, 0, 0])
     assert_same(got, ref)
 
 
-def test_history_out_of_range_is_reported(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_history_out_of_range_is_reported(sv, path):
     x = torch.zeros((2, 1000), device=DEV)
     hist = torch.tensor([[1, 2, 3], [4, 1000, 5]], dtype=torch.int32, device=DEV)
-    out = sv.sample_step(x, torch.zeros(2, device=DEV), history=hist)
+    out = sv.sample_step(x, torch.zeros(2, device=DEV), history=hist, path=path)
     assert out["status"].tolist() == [0, 4]
     assert out["token"].tolist()[1] == -1
 
 
-def test_broadcast_row_and_misaligned_base(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_broadcast_row_and_misaligned_base(sv, path):
     """Stride-0 rows (the prefill's expand, runtime_1b.py:82) and rows that start
     off the 16-byte grid (an offset view)."""
     g = np.random.default_rng(9)
@@ -191,24 +204,26 @@ def test_broadcast_row_and_misaligned_base(sv):
     seen = torch.zeros((4, 49157), dtype=torch.bool, device=DEV)
     seen[1, :500] = True
     u = to_dev(g.random(4).astype(np.float32))
-    out = sv.sample_step(x, u, seen=seen, out_capacity=64)
+    out = sv.sample_step(x, u, seen=seen, out_capacity=64, path=path)
     xn = np.repeat(x[:1].cpu().numpy(), 4, 0)
     ref = O.sample(xn, u.cpu().numpy(), seen=seen.cpu().numpy(), cap=64)
     np.testing.assert_array_equal(out["token"].cpu().numpy(), ref["token"])
     np.testing.assert_array_equal(out["prob"].cpu().numpy(), ref["prob"])
     x2 = base[3:3 + 3 * 49151].reshape(3, 49151)
     xh = x2.half()[:, 1:]
-    out = sv.sample_step(xh, u[:3], out_capacity=64)
+    out = sv.sample_step(xh, u[:3], out_capacity=64, path=path)
     ref = O.sample(xh.float().cpu().numpy(), u[:3].cpu().numpy(), cap=64)
     np.testing.assert_array_equal(out["token"].cpu().numpy(), ref["token"])
     np.testing.assert_array_equal(out["prob"].cpu().numpy(), ref["prob"])
 
 
-def test_seen_update_in_kernel(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_seen_update_in_kernel(sv, path):
     g = np.random.default_rng(10)
     x = to_dev((2 * g.standard_normal((5, 3000))).astype(np.float32))
     bits = sv.seen_bitmap(5, 3000, DEV)
-    out = sv.sample_step(x, to_dev(g.random(5).astype(np.float32)), seen_bits=bits, update_seen_bits=bits)
+    out = sv.sample_step(x, to_dev(g.random(5).astype(np.float32)), seen_bits=bits, update_seen_bits=bits,
+                         path=path)
     tok = out["token"].cpu().numpy()
     b = bits.cpu().numpy().view(np.uint32)
     for r in range(5):
@@ -216,29 +231,32 @@ def test_seen_update_in_kernel(sv):
         assert set_bits == [tok[r]]
 
 
-def test_uniform_edges_select_first_and_last(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_uniform_edges_select_first_and_last(sv, path):
     g = np.random.default_rng(12)
     x = (2 * g.standard_normal((2, 4000))).astype(np.float32)
     u = np.array([0.0, np.nextafter(np.float32(1), np.float32(0))], np.float32)
-    got, ref = run_both(sv, x, u, cap=100)
+    got, ref = run_both(sv, x, u, cap=100, path=path)
     assert_same(got, ref)
     n = got["count"]
     assert got["token"][0] == got["idx"][0, 0]
     assert got["token"][1] == got["idx"][1, n[1] - 1]
 
 
-def test_cfg1_full_size(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_cfg1_full_size(sv, path):
     d = bench.cfg1()
-    got, ref = run_both(sv, d["logits"], d["uniforms"], ids=d["history"], cap=256)
+    got, ref = run_both(sv, d["logits"], d["uniforms"], ids=d["history"], cap=256, path=path)
     assert_same(got, ref)
 
 
-def test_cfg4_full_size_against_oracle(sv):
+@pytest.mark.parametrize("path", PATHS)
+def test_cfg4_full_size_against_oracle(sv, path):
     """Config 4 at its full size: 1024 rows x 49152, Zipf histories; every row
     bit-exact against the oracle, plus size-independent properties."""
     d = bench.cfg4()
     x, h, u = d["logits"], d["history"], d["uniforms"]
-    out = sv.sample_step(to_dev(x), to_dev(u), history=to_dev(h), out_capacity=128)
+    out = sv.sample_step(to_dev(x), to_dev(u), history=to_dev(h), out_capacity=128, path=path)
     torch.cuda.synchronize()
     got = {k: v.cpu().numpy() for k, v in out.items()}
     ref = O.sample(x, u, ids=h, cap=128)
