@@ -361,21 +361,23 @@ __device__ int prefilter(BlockScratch<NT>& bs, const float* cv, const int* ci, i
 
 // Top-k threshold with ties, top-p and the index-ordered kept list from n
 // candidates (in_val, in_idx), which must contain every entry >= the k-th largest.
-//   sval, sidx: n floats / ints; W: n u64 (may alias in_val/in_idx); P: n u64.
-//   kidx, kval: the kept list (may alias P).
+//   sval, sidx: n floats / ints; W: n u64 (may alias in_val/in_idx); P: n u64 (must
+//   not alias in_val/in_idx).  kidx, kval: the kept list (may alias P).
 template <int NT>
 __device__ Kept leader_fast(const RowArgs& a, BlockScratch<NT>& bs, const float* in_val, const int* in_idx, int n,
                             float* sval, int* sidx, uint64_t* W, uint64_t* P, int* kidx, float* kval) {
   const int tid = threadIdx.x;
-  // (a) ascending order by (value, index): rank counting over ordered keys.
+  // (a) ascending order by (value, index): rank counting over 64-bit ordered keys
+  //     (distinct, since indices are), staged in P.
+  for (int t = tid; t < n; t += NT) P[t] = ((uint64_t)ord_key(in_val[t]) << 32) | (uint32_t)in_idx[t];
+  __syncthreads();
   for (int t = tid; t < n; t += NT) {
-    const float vt = in_val[t];
-    const int it = in_idx[t];
-    const uint64_t kt = ((uint64_t)ord_key(vt) << 32) | (uint32_t)it;
-    int rank = 0;
-    for (int j = 0; j < n; ++j) rank += (((uint64_t)ord_key(in_val[j]) << 32) | (uint32_t)in_idx[j]) < kt;
-    sval[rank] = vt;
-    sidx[rank] = it;
+    const uint64_t kt = P[t];
+    int rank = 0, j = 0;
+    for (; j + 4 <= n; j += 4) rank += (P[j] < kt) + (P[j + 1] < kt) + (P[j + 2] < kt) + (P[j + 3] < kt);
+    for (; j < n; ++j) rank += P[j] < kt;
+    sval[rank] = in_val[t];
+    sidx[rank] = in_idx[t];
   }
   __syncthreads();
   // (b) exact k-th largest with ties: survivors are sorted positions [f0, n).

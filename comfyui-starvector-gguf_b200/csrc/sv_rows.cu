@@ -439,8 +439,12 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
       base = __shfl_sync(0xffffffffu, base, ll);
       if (pass[e]) {
         const int slot = base + __popc(bm & lt_mask);
+        const float tv = temper(v[e], T);
+        // A finite score the temperature takes to +inf (T < 1); every element at
+        // or above the bound is tested, so the largest ones always are.
+        if (tv == __int_as_float(0x7f800000)) atomicOr(remote(cluster, &sh.err, 0), 1 << ST_POSINF);
         if (slot < CAP) {
-          rval[slot] = temper(v[e], T);
+          rval[slot] = tv;
           ridx[slot] = (int)(lo + (int64_t)(u * EPU + e) - off_e);
         }
       }

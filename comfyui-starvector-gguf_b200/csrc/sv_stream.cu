@@ -8,20 +8,25 @@
 //
 // Per row (runtime_shared.py:200-202):
 //   1. the row's seen bitmap in shared memory, from the history;
-//   2. per chunk, one pass: repetition penalty (:172-173), the candidate test
-//      against the current lower bound tau of the row's k-th largest penalised
-//      score, and the maxima of 128 lane groups.  The first chunk is read twice:
-//      the exact k-th largest of its group maxima is the first bound.  Later group
-//      maxima go into a 256-bin histogram over ordered float keys above that bound;
-//      the highest bin edge with at least k group maxima at or above it is a valid,
-//      tightening bound (group maxima of disjoint groups are distinct elements).
-//      Candidates are tempered (:178-179) and appended to the row's list;
-//   3. finish: candidates below the final bound are dropped, then the exact k-th
-//      largest with ties (:180-181), top-p over the ascending (value, index) order
-//      with exact fixed-point mass (:182-186) and the draw from the row's uniform.
-//      A row with too many candidates (huge tie groups) takes the general path
-//      over the whole row.
-// No inter-CTA communication and no scratch memory in global memory.
+//   2. per chunk, one pass over 16-byte units: the unit maximum of the raw scores
+//      is tested against the current lower bound tau of the row's k-th largest
+//      penalised score; only units that pass are re-read element by element, with
+//      the repetition penalty (:172-173), and their elements >= tau appended to the
+//      row's candidates.  The units also feed 128 lane-pair group maxima, a seen
+//      element through a lower bound of its penalised score (group maxima of
+//      disjoint groups are distinct elements, each at or above its group's value,
+//      so their k-th largest bounds the row's k-th largest from below).  In the
+//      first chunk each warp's r-th largest group maximum (r = ceil(k/8)) gives
+//      the first bound; later group maxima go into a 256-bin histogram over
+//      ordered float keys, whose highest bin edge with at least k maxima at or
+//      above it is a tightening bound;
+//   3. finish: candidates below the final bound are dropped and the rest tempered
+//      (:178-179); then the exact k-th largest with ties (:180-181), top-p over the
+//      ascending (value, index) order with exact fixed-point mass (:182-186) and
+//      the draw from the row's uniform.  A row with too many candidates (huge tie
+//      groups) takes the general path over the whole row.
+// Status: a NaN anywhere in the row, else a +inf tempered score, else no finite
+// score.  No inter-CTA communication and no scratch memory in global memory.
 #include <cuda_runtime.h>
 
 #include "sv_block.cuh"
@@ -32,27 +37,28 @@ namespace sv {
 
 namespace {
 
-constexpr int SNT = 256;               // threads per CTA
-constexpr int SBUF = 3;                // ring slots
-constexpr int SCHUNK = 16 * 1024;      // bytes per slot / chunk
-constexpr int SCU = SCHUNK / 16;       // 16-byte units per chunk
-constexpr int UPT = SCU / SNT;         // units per thread per chunk
-constexpr int SG = 128;                // group maxima per chunk (groups of 2 lanes)
-constexpr int SBINS = 256;             // bound histogram bins
-constexpr int SCAP = kCandCap;         // candidates per row
-constexpr int SFIN = 256;              // candidates the fast finish handles after pruning
+constexpr int SNT = 256;                // threads per CTA
+constexpr int SWARPS = SNT / 32;
+constexpr int SBUF = 3;                 // ring slots
+constexpr int SCHUNK = 16 * 1024;       // bytes per slot / chunk
+constexpr int SCU = SCHUNK / 16;        // 16-byte units per chunk
+constexpr int UPT = SCU / SNT;          // units per thread per chunk
+constexpr int SBINS = 256;              // bound histogram bins
+constexpr int SCAP = kCandCap;          // candidates per row
+constexpr int SFIN = 256;               // candidates the fast finish handles after pruning
+constexpr int kBoundWarp = SWARPS - 1;  // computes the histogram bound after each chunk
 
 struct __align__(16) StreamShared {
   unsigned long long mbar[SBUF];
   BlockScratch<SNT> bs;
-  float gmax[SG];
-  unsigned int bins[SBINS];
-  unsigned int base_key;
-  int bin_shift;
-  float te_pub;  // bound published by warp 0 for the chunk after next
+  __align__(16) unsigned int bins[SBINS];
+  float wsel[SWARPS];     // first chunk: each warp's r-th largest group maximum
+  float wtop[SWARPS];     //              and its largest
+  float te_pub;           // bound published by the bound warp, read after the next barrier
+  unsigned int rmax_key;  // ordered key of the row's largest raw score
   int cand_n;
   int err;
-  __align__(16) float cand_val[SCAP];
+  __align__(16) float cand_val[SCAP];  // penalised (not yet tempered) scores
   int cand_idx[SCAP];
   __align__(16) unsigned char work[16 * SFIN];  // finish arrays / general-path scratch
 };
@@ -116,17 +122,18 @@ __device__ __forceinline__ uint32_t unit_bits(const uint32_t* bm, int64_t e0, in
   return r;
 }
 
-// The bound from the histogram, computed by each warp on its own (identical in
-// every warp): the highest bin b with at least kk group maxima in bins >= b gives
-// key base + (b << shift).  Returns the lowered bound in the penalised domain.
-__device__ __forceinline__ float hist_bound(const StreamShared& sh, int kk, float T) {
+// The bound from the histogram (one warp): the highest bin b with at least kk group
+// maxima in bins >= b gives key base + (b << shift).  Returns the lowered bound in
+// the penalised domain, or -inf.  Lane l reads bins 8l .. 8l+7.
+__device__ __forceinline__ float hist_bound(const unsigned int* bins, uint32_t base_key, int shift, int kk,
+                                            float T) {
   const int lane = threadIdx.x & 31;
-  uint32_t c[8], s = 0;
+  const uint4 b0 = reinterpret_cast<const uint4*>(bins)[2 * lane];
+  const uint4 b1 = reinterpret_cast<const uint4*>(bins)[2 * lane + 1];
+  const uint32_t c[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  uint32_t s = 0;
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    c[q] = sh.bins[lane * 8 + q];
-    s += c[q];
-  }
+  for (int q = 0; q < 8; ++q) s += c[q];
   uint32_t incl = s;  // count in bins of lanes >= lane
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -134,50 +141,42 @@ __device__ __forceinline__ float hist_bound(const StreamShared& sh, int kk, floa
     if (lane + o < 32) incl += t;
   }
   int best = -1;
-  if (incl >= (uint32_t)kk) {
-    uint32_t above = incl - s;
-    for (int q = 7; q >= 0; --q) {
-      above += c[q];
-      if (above >= (uint32_t)kk) {
-        best = lane * 8 + q;
-        break;
-      }
-    }
+  uint32_t above = incl - s;
+#pragma unroll
+  for (int q = 7; q >= 0; --q) {
+    above += c[q];
+    if (best < 0 && above >= (uint32_t)kk) best = lane * 8 + q;
   }
   // The highest lane with a qualifying bin holds the answer.
   const unsigned m = __ballot_sync(0xffffffffu, best >= 0);
-  const int src = m ? 31 - __clz(m) : 0;
-  best = __shfl_sync(0xffffffffu, best, src);
-  if (best < 0) return Elem<float>::neg_inf();
-  const uint32_t k = sh.base_key + ((uint32_t)best << sh.bin_shift);
-  return lower_tau(key_to_float(k), T);
+  if (!m) return Elem<float>::neg_inf();
+  best = __shfl_sync(0xffffffffu, best, 31 - __clz(m));
+  return lower_tau(key_to_float(base_key + ((uint32_t)best << shift)), T);
 }
 
-// k-th largest (kk <= SG) of the SG group maxima by one warp: a bitwise radix
-// select over ordered keys with ballots.  Returns the raw value (all lanes) and
-// ORs NaN / +inf error bits into *err (lane 0).
-__device__ __forceinline__ float warp_kth_of_groups(const float* g, int kk, int* err) {
-  const int lane = threadIdx.x & 31;
-  uint32_t k4[4];
-  bool nan = false, pinf = false;
+// Marks history ids staged in shared memory (16-byte vectors of Id) in the bitmap;
+// returns the ST_HISTORY error bit for ids outside [0, V).
+template <typename Id>
+__device__ __forceinline__ int mark_staged(const unsigned char* src, int64_t L, int64_t V, uint32_t* bits) {
+  constexpr int PER = 16 / (int)sizeof(Id);
+  int err = 0;
+  for (int64_t q = threadIdx.x; q * PER < L; q += SNT) {
+    Id id[PER];
+    *reinterpret_cast<uint4*>(id) = reinterpret_cast<const uint4*>(src)[q];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float v = g[lane * 4 + q];
-    nan |= v != v;
-    pinf |= v == __int_as_float(0x7f800000);
-    k4[q] = ord_key(v);
+    for (int t = 0; t < PER; ++t) {
+      if (q * PER + t >= L) break;
+      const int64_t x = (int64_t)id[t];
+      if (x < 0 || x >= V) {
+        err |= 1 << ST_HISTORY;
+      } else {
+        const uint32_t b = 1u << (x & 31);
+        uint32_t* w = &bits[x >> 5];
+        if (!(*w & b)) atomicOr(w, b);  // repeated ids mostly find their bit set
+      }
+    }
   }
-  nan = __any_sync(0xffffffffu, nan);
-  pinf = __any_sync(0xffffffffu, pinf);
-  uint32_t res = 0;
-  for (int b = 31; b >= 0; --b) {
-    const uint32_t c = res | (1u << b);
-    const int n = __popc(__ballot_sync(0xffffffffu, k4[0] >= c)) + __popc(__ballot_sync(0xffffffffu, k4[1] >= c)) +
-                  __popc(__ballot_sync(0xffffffffu, k4[2] >= c)) + __popc(__ballot_sync(0xffffffffu, k4[3] >= c));
-    if (n >= kk) res = c;
-  }
-  if (lane == 0 && (nan || pinf)) atomicOr(err, 1 << (nan ? ST_NAN : ST_POSINF));
-  return key_to_float(res);
+  return err;
 }
 
 template <typename TIn>
@@ -190,11 +189,13 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
   constexpr int ES = Elem<TIn>::kSize;
   constexpr int EPU = 16 / ES;
   using IO = UnitIO<TIn>;
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float NEG = Elem<float>::neg_inf();
+  const float PINF = __int_as_float(0x7f800000);
   const int64_t V = a.vocab;
   const int nw = (int)((V + 31) >> 5);
   const float rp = a.rep_penalty, T = a.temperature;
+  const float rinv_lo = __frcp_rd(rp);  // <= 1/rp: x * rinv_lo rounded down <= x / rp rounded
   const int kk = a.kk;
   const int64_t first = blockIdx.x, step = gridDim.x;
   if (first >= a.rows) return;
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
   int64_t irow = first;
   int ic = stage_ids ? -1 : 0;
   RowGeom ig = row_geom<TIn>(a, irow);
-  int64_t issued = 0;
+  int islot = 0;  // ring slot of the next issue
   if (tid == 0) {
     for (int s = 0; s < SBUF; ++s) mbar_init(&sh.mbar[s], 1);
     mbar_init_fence();
@@ -220,7 +221,7 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
   auto issue_next = [&]() {  // thread 0, after a block barrier
     if (irow >= a.rows) return;
     fence_proxy_async_smem();
-    const int s = (int)(issued % SBUF);
+    const int s = islot;
     unsigned char* slot = ring + (size_t)s * SCHUNK;
     if (ic < 0) {
       mbar_expect_tx(&sh.mbar[s], (uint32_t)hbytes);
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
     } else {
       issue_chunk(ig, ic, slot, &sh.mbar[s]);
     }
-    ++issued;
+    if (++islot == SBUF) islot = 0;
     if (++ic == ig.nch) {
       ic = stage_ids ? -1 : 0;
       irow += step;
@@ -239,58 +240,52 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
   if (tid == 0)
     for (int s = 0; s < SBUF; ++s) issue_next();
 
-  int64_t consumed = 0;  // slots consumed so far (all threads)
+  // Ring slot and mbarrier phase of the next slot to consume (all threads).
+  int cslot = 0;
+  uint32_t cphase = 0;
+  auto consume_next = [&]() {
+    if (++cslot == SBUF) {
+      cslot = 0;
+      cphase ^= 1u;
+    }
+  };
+
   for (int64_t row = first; row < a.rows; row += step) {
     const RowGeom g = row_geom<TIn>(a, row);
     const TIn* rowp = reinterpret_cast<const TIn*>(a.logits) + row * a.row_stride;
     const bool aligned = g.off_e == 0;
     // 1. seen bitmap of the row.
-    for (int w = tid; w < nw + 4; w += SNT) bits[w] = 0;
-    for (int b = tid; b < SBINS; b += SNT) sh.bins[b] = 0;
+    {
+      const int nz = (nw + 4 + 3) >> 2;  // 16-byte words, within bitmap_bytes(V)
+      for (int w = tid; w < nz; w += SNT) reinterpret_cast<uint4*>(bits)[w] = make_uint4(0, 0, 0, 0);
+    }
+    if (tid < SBINS / 4) reinterpret_cast<uint4*>(sh.bins)[tid] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
       sh.cand_n = 0;
       sh.te_pub = NEG;
+      sh.rmax_key = 0;
     }
     __syncthreads();
     int local_err = 0;
     if (ids_kind) {
       const int64_t L = hist_length(a, row);
-      const void* src;
-      int64_t s = -1;
       if (stage_ids) {
-        s = consumed % SBUF;
-        if (!mbar_wait(&sh.mbar[s], (uint32_t)((consumed / SBUF) & 1))) local_err |= 1 << ST_TIMEOUT;
-        src = ring + (size_t)s * SCHUNK;
-      } else {
-        src = reinterpret_cast<const unsigned char*>(a.hist) + (size_t)row * a.hist_stride * idb;
-      }
-      constexpr int U = 8;
-      for (int64_t base = 0; base < L; base += (int64_t)SNT * U) {
-        int64_t id[U];
-#pragma unroll
-        for (int q = 0; q < U; ++q) {
-          const int64_t j = base + tid + (int64_t)q * SNT;
-          id[q] = j >= L ? 0
-                         : (idb == 4 ? (int64_t) reinterpret_cast<const int32_t*>(src)[j]
-                                     : reinterpret_cast<const int64_t*>(src)[j]);
-        }
-#pragma unroll
-        for (int q = 0; q < U; ++q) {
-          const int64_t j = base + tid + (int64_t)q * SNT;
-          if (j >= L) continue;
-          if (id[q] < 0 || id[q] >= V) {
-            local_err |= 1 << ST_HISTORY;
-            continue;
-          }
-          const uint32_t b = 1u << (id[q] & 31);
-          uint32_t* w = &bits[id[q] >> 5];
-          if (!(*w & b)) atomicOr(w, b);  // repeated ids mostly find their bit set
-        }
-      }
-      if (stage_ids) {
-        ++consumed;
+        if (!mbar_wait(&sh.mbar[cslot], cphase)) local_err |= 1 << ST_TIMEOUT;
+        const unsigned char* src = ring + (size_t)cslot * SCHUNK;
+        local_err |= idb == 4 ? mark_staged<int32_t>(src, L, V, bits) : mark_staged<int64_t>(src, L, V, bits);
+        consume_next();
         __syncthreads();  // the ids slot is consumed
         if (tid == 0) issue_next();
+      } else {
+        for (int64_t j = tid; j < L; j += SNT) {
+          const int64_t x = hist_id(a, row, j);
+          if (x < 0 || x >= V) {
+            local_err |= 1 << ST_HISTORY;
+          } else {
+            const uint32_t b = 1u << (x & 31);
+            if (!(bits[x >> 5] & b)) atomicOr(&bits[x >> 5], b);
+          }
+        }
       }
     } else if (a.hist_kind == HIST_BITS32) {
       const uint32_t* hb = reinterpret_cast<const uint32_t*>(a.hist) + row * a.hist_stride;
@@ -307,11 +302,13 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
     __syncthreads();
 
     // 2. chunks.
-    float te = NEG;
-    for (int c = 0; c < g.nch; ++c, ++consumed) {
-      const int s = (int)(consumed % SBUF);
-      TIn* slot = reinterpret_cast<TIn*>(ring + (size_t)s * SCHUNK);
-      if (!mbar_wait(&sh.mbar[s], (uint32_t)((consumed / SBUF) & 1))) atomicOr(&sh.err, 1 << ST_TIMEOUT);
+    float te = NEG;         // current bound (penalised domain)
+    float rmx = NEG;        // NaN-propagating maximum of this thread's raw scores
+    uint32_t base_key = 0;  // histogram origin and bin width (identical in all threads)
+    int bin_shift = 0;
+    for (int c = 0; c < g.nch; ++c, consume_next()) {
+      TIn* slot = reinterpret_cast<TIn*>(ring + (size_t)cslot * SCHUNK);
+      if (!mbar_wait(&sh.mbar[cslot], cphase)) atomicOr(&sh.err, 1 << ST_TIMEOUT);
       const int u0 = c * SCU;
       const int un = min(SCU, g.nunits - u0);
       // Ragged units (outside the aligned interior) come from global memory, with
@@ -328,140 +325,141 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
           }
         }
       }
-      const bool two_pass = c == 0;
-      // Seen-bit lookup: for aligned rows each of this thread's units sits at a fixed
-      // bit offset in consecutive bitmap words.
-      const int ubase = u0 + tid;
-      for (int pass = two_pass ? 0 : 1; pass < 2; ++pass) {
-        const bool collect = pass == 1;
-        const bool groups = !(collect && two_pass);
-        // One compare excludes -inf and keeps every finite value >= te.
-        const float tcmp = fmaxf(te, -3.402823466e38f);
-        float v[UPT][EPU];
-        uint32_t sb[UPT];
+      // Unit maxima, seen bits and this lane's group value.  For aligned rows this
+      // thread's units sit at a fixed bit offset in consecutive bitmap words.
+      float umax[UPT];
+      uint32_t sb[UPT];
+      float gsrc = NEG;
 #pragma unroll
-        for (int j = 0; j < UPT; ++j) {
-          const int k = tid + j * SNT;
-          if (k < un) {
-            IO::load(slot, k, v[j]);
-          } else {
-#pragma unroll
-            for (int e = 0; e < EPU; ++e) v[j][e] = NEG;
-          }
-        }
+      for (int j = 0; j < UPT; ++j) {
+        const int k = tid + j * SNT;
+        float m = NEG, gv = NEG;
         if (aligned) {
-          const int shift = (ubase * EPU) & 31;
-#pragma unroll
-          for (int j = 0; j < UPT; ++j) {
-            const int k = tid + j * SNT;
-            sb[j] = k < un ? (bits[((ubase + j * SNT) * EPU) >> 5] >> shift) & ((1u << EPU) - 1u) : 0u;
-          }
+          sb[j] = k < un ? (bits[((u0 + k) * EPU) >> 5] >> (((u0 + k) * EPU) & 31)) & ((1u << EPU) - 1u) : 0u;
         } else {
+          sb[j] = k < un ? unit_bits(bits, (int64_t)(u0 + k) * EPU - g.off_e, EPU, V) : 0u;
+        }
+        if (k < un) {
+          float v[EPU];
+          IO::load(slot, k, v);
+          m = v[0];
 #pragma unroll
-          for (int j = 0; j < UPT; ++j) {
-            const int k = tid + j * SNT;
-            sb[j] = k < un ? unit_bits(bits, (int64_t)(u0 + k) * EPU - g.off_e, EPU, V) : 0u;
+          for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
+          gv = m;
+          if (sb[j]) {
+            // Seen elements enter the group value through a lower bound of their
+            // penalised score (products rounded down), which needs no division.
+            gv = NEG;
+#pragma unroll
+            for (int e = 0; e < EPU; ++e) {
+              const float lo = v[e] < 0.0f ? __fmul_rd(v[e], rp) : __fmul_rd(v[e], rinv_lo);
+              gv = fmaxf(gv, ((sb[j] >> e) & 1u) ? lo : v[e]);
+            }
           }
         }
-        float tmax = NEG;
-        uint32_t hits = 0;
+        umax[j] = m;
+        rmx = max_nan(rmx, m);
+        gsrc = fmaxf(gsrc, gv);  // fmaxf drops NaN; rmx reports it
+      }
+      const float gm = fmaxf(gsrc, __shfl_xor_sync(0xffffffffu, gsrc, 1));  // lane-pair group value
+      if (c == 0) {
+        // First bound: each warp's r-th largest of its 16 group values (ties by
+        // group), r = ceil(kk / 8): 8r >= kk distinct elements lie at or above the
+        // smallest of them.
+        const int pair = lane >> 1;
+        int rank = 0;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float w = __shfl_sync(0xffffffffu, gm, 2 * q);
+          rank += (w > gm) || (w == gm && q < pair);
+        }
+        const unsigned sel = __ballot_sync(0xffffffffu, rank == ((kk + 7) >> 3) - 1);
+        const unsigned top = __ballot_sync(0xffffffffu, rank == 0);
+        const float wsel = __shfl_sync(0xffffffffu, gm, __ffs(sel) - 1);
+        const float wtop = __shfl_sync(0xffffffffu, gm, __ffs(top) - 1);
+        if (lane == 0) {
+          sh.wsel[warp] = wsel;
+          sh.wtop[warp] = wtop;
+        }
+        __syncthreads();
+        float raw = sh.wsel[0], hi = sh.wtop[0];
+#pragma unroll
+        for (int w = 1; w < SWARPS; ++w) {
+          raw = fminf(raw, sh.wsel[w]);
+          hi = fmaxf(hi, sh.wtop[w]);
+        }
+        base_key = ord_key(raw);
+        const uint32_t span = ord_key(hi) > base_key ? ord_key(hi) - base_key : 0u;
+        bin_shift = 0;
+        while ((span >> bin_shift) >= (uint32_t)SBINS) ++bin_shift;
+        te = lower_tau(raw, T);
+      }
+      // Candidates: units whose maximum reaches the bound, element by element.
+      const float tcmp = fmaxf(te, -3.402823466e38f);  // excludes -inf
+      uint32_t hu = 0;
+#pragma unroll
+      for (int j = 0; j < UPT; ++j) hu |= (uint32_t)(umax[j] >= tcmp) << j;
+      if (hu) {
 #pragma unroll
         for (int j = 0; j < UPT; ++j) {
-          if (sb[j]) {
+          if ((hu >> j) & 1u) {
+            const int k = tid + j * SNT;
+            float v[EPU];
+            IO::load(slot, k, v);
+            if (sb[j]) {
 #pragma unroll
-            for (int e = 0; e < EPU; ++e)
-              if ((sb[j] >> e) & 1u) v[j][e] = penalize(v[j][e], rp);
-          }
-#pragma unroll
-          for (int e = 0; e < EPU; ++e) {
-            if (groups) tmax = max_nan(tmax, v[j][e]);
-            if (collect) hits |= (uint32_t)(v[j][e] >= tcmp) << (j * EPU + e);
-          }
-        }
-        if (collect && __any_sync(0xffffffffu, hits != 0)) {
-          // One atomic per warp: lanes' hit counts are scanned, then written.
-          const int cnt = __popc(hits);
-          int incl = cnt;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
-          }
-          int base = 0;
-          if (lane == 31) base = atomicAdd(&sh.cand_n, incl);
-          base = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
-          // Hits are re-read from the slot (a register array indexed at run time would
-          // live in local memory); a hit is a finite element inside the row.
-          while (hits) {
-            const int q = __ffs(hits) - 1;
-            hits &= hits - 1;
-            const int k = tid + (q / EPU) * SNT, e = q % EPU;
-            const int i = (u0 + k) * EPU + e - g.off_e;
-            float x = Elem<TIn>::to_f(slot[k * EPU + e]);
-            if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
-            if (base < SCAP) {
-              sh.cand_val[base] = temper(x, T);
-              sh.cand_idx[base] = i;
+              for (int e = 0; e < EPU; ++e)
+                if ((sb[j] >> e) & 1u) v[e] = penalize(v[e], rp);
             }
-            ++base;
-          }
-        }
-        if (groups) {
-          tmax = max_nan(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-          if (two_pass) {
-            // First chunk: the exact k-th largest of its group maxima anchors the bins.
-            if ((tid & 1) == 0) sh.gmax[tid >> 1] = tmax;
-            __syncthreads();
-            if (tid < 32) {
-              const float raw = warp_kth_of_groups(sh.gmax, kk, &sh.err);
-              float top = NEG;
+            uint32_t m = 0;
 #pragma unroll
-              for (int q = 0; q < 4; ++q) top = fmaxf(top, sh.gmax[lane * 4 + q]);
+            for (int e = 0; e < EPU; ++e) m |= (uint32_t)(v[e] >= tcmp) << e;
+            if (m) {
+              int pos = atomicAdd(&sh.cand_n, __popc(m));
+              const int i0 = (u0 + k) * EPU - g.off_e;
 #pragma unroll
-              for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, o));
-              if (lane == 0) {
-                const uint32_t base = ord_key(raw);
-                const uint32_t span = ord_key(top) > base ? ord_key(top) - base : 0u;
-                int shf = 0;
-                while ((span >> shf) >= (uint32_t)SBINS) ++shf;
-                sh.base_key = base;
-                sh.bin_shift = shf;
-                sh.te_pub = lower_tau(raw, T);
+              for (int e = 0; e < EPU; ++e) {
+                if ((m >> e) & 1u) {
+                  if (pos < SCAP) {
+                    sh.cand_val[pos] = v[e];
+                    sh.cand_idx[pos] = i0 + e;
+                  }
+                  ++pos;
+                }
               }
-            }
-            __syncthreads();
-            te = sh.te_pub;
-          }
-          if ((tid & 1) == 0) {
-            if (tmax != tmax) atomicOr(&sh.err, 1 << ST_NAN);
-            else if (tmax == __int_as_float(0x7f800000)) atomicOr(&sh.err, 1 << ST_POSINF);
-            else {
-              const uint32_t k = ord_key(tmax);
-              if (k >= sh.base_key) atomicAdd(&sh.bins[min((uint32_t)(SBINS - 1), (k - sh.base_key) >> sh.bin_shift)], 1u);
             }
           }
         }
       }
-      __syncthreads();  // the slot is consumed; the bins hold this chunk's maxima
-      // The bound published during the previous chunk (bins complete up to the chunk
-      // before it); warp 0 then publishes one from the bins complete up to this chunk,
-      // read after the next chunk's barrier.
+      // Histogram of the group values that can still raise the bound.
+      if ((lane & 1) == 0) {
+        const uint32_t k = ord_key(gm);
+        if (gm >= te && k >= base_key)
+          atomicAdd(&sh.bins[min((uint32_t)(SBINS - 1), (k - base_key) >> bin_shift)], 1u);
+      }
+      __syncthreads();  // the slot is consumed; the bins hold this chunk's values
+      // The bound published during the previous chunk; the bound warp then publishes
+      // one from the bins complete up to this chunk.  (A thread may read either: both
+      // are valid bounds.)
       te = fmaxf(te, sh.te_pub);
-      if (tid < 32) {
-        const float tb = hist_bound(sh, kk, T);
-        __syncwarp();
+      if (warp == kBoundWarp) {
+        const float tb = hist_bound(sh.bins, base_key, bin_shift, kk, T);
         if (lane == 0) sh.te_pub = tb;
       }
       if (tid == 0) issue_next();
     }
 
     // 3. finish the row.
+    if (rmx != rmx) atomicOr(&sh.err, 1 << ST_NAN);
+    else if (rmx == PINF) atomicOr(&sh.err, 1 << ST_POSINF);
+    rmx = warp_max_nan(rmx);
+    if (lane == 0 && rmx == rmx) atomicMax(&sh.rmax_key, ord_key(rmx));
+    if (tid == 0) bs.flag = 0;
+    __syncthreads();
+    const float tfin = fmaxf(te, sh.te_pub);
     const float uu = a.uniforms[row];
-    int status = sh.err ? first_err(sh.err) : ST_OK;
     const int n = sh.cand_n;
-    if (status == ST_OK && n == 0) status = ST_ALLNEGINF;
-    Kept kept = {0, 0.0f, 0};
-    int64_t token = -1;
+    int status = sh.err ? first_err(sh.err) : ST_OK;
     bool general = status == ST_OK && (a.force_slow || n > SCAP);
     float* sval = reinterpret_cast<float*>(sh.work);
     int* sidx = reinterpret_cast<int*>(sh.work + 4 * SFIN);
@@ -470,25 +468,43 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
     int* fi = reinterpret_cast<int*>(sh.work + 12 * SFIN);
     int m = 0;
     if (status == ST_OK && !general) {
-      // Drop candidates below the final bound (monotone in the tempered domain).
-      const float tft = te == NEG ? NEG : __fdiv_rn(te, T);
-      if (tid == 0) bs.flag = 0;
-      __syncthreads();
+      // Drop candidates below the final bound, temper the rest.
+      int bad = 0;
       for (int t = tid; t < n; t += SNT) {
         const float v = sh.cand_val[t];
-        if (v >= tft) {
+        if (v >= tfin) {
+          const float x = temper(v, T);
+          bad |= x == PINF;
           const int at = atomicAdd(&bs.flag, 1);
           if (at < SFIN) {
-            fv[at] = v;
+            fv[at] = x;
             fi[at] = sh.cand_idx[t];
           }
         }
       }
+      if (bad) atomicOr(&sh.err, 1 << ST_POSINF);
       __syncthreads();
       m = bs.flag;
+      if (sh.err) status = first_err(sh.err);
       __syncthreads();
-      if (m > SFIN) general = true;
+      if (m > SFIN) general = status == ST_OK;
     }
+    if (general && temper(key_to_float(sh.rmax_key), T) == PINF) {
+      // A score may reach +inf only through the temperature: check every element.
+      int inf = 0;
+      for (int64_t i = tid; i < V; i += SNT) {
+        float x = Elem<TIn>::load(rowp + i);
+        if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
+        inf |= temper(x, T) == PINF;
+      }
+      if (__syncthreads_or(inf)) {
+        status = ST_POSINF;
+        general = false;
+      }
+    }
+    if (status == ST_OK && !general && m == 0) status = ST_ALLNEGINF;
+    Kept kept = {0, 0.0f, 0};
+    int64_t token = -1;
     if (a.out_dense && a.dense_mode != DENSE_NONE && status == ST_OK && !general) {
       const float dv = a.dense_mode == DENSE_SCORES ? NEG : 0.0f;
       for (int64_t i = tid; i < V; i += SNT) a.out_dense[row * a.dense_stride + i] = dv;

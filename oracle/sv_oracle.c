@@ -207,16 +207,21 @@ static void work_free(work_t *w)
 static int warp_row(work_t *w, float *s, int64_t V, const uint8_t *seen, float T, float rp,
                     float pthr, int kk, int keep, float *pmax)
 {
+    /* A NaN anywhere in the row takes precedence over +inf (either makes the
+     * reference's multinomial raise; the status only names the cause). */
+    int any_nan = 0, any_inf = 0;
     for (int64_t i = 0; i < V; i++) {
         float v = s[i];
         if (seen && seen[i]) v = (v < 0.0f) ? v * rp : v / rp;
         /* Temperature, then -0 -> +0: torch compares -0 == +0, and the canonical
          * zero keeps the ordered-key sort consistent with float comparisons. */
         v = v / T + 0.0f;
-        if (v != v) return ORC_ERR_NAN;
-        if (v == INFINITY) return ORC_ERR_POSINF;
+        any_nan |= v != v;
+        any_inf |= v == INFINITY;
         s[i] = v;
     }
+    if (any_nan) return ORC_ERR_NAN;
+    if (any_inf) return ORC_ERR_POSINF;
     memcpy(w->sel, s, (size_t)V * 4);
     float thr = kth_largest(w->sel, V, kk);
     float M = -INFINITY;
@@ -403,12 +408,13 @@ int orc_beam(const float *logits, int64_t B, int64_t V, int64_t row_stride, cons
     for (int64_t b = 0; b < B && st == ORC_OK; b++) {
         const float *x = logits + b * row_stride;
         float M = -INFINITY;
+        int any_nan = 0, any_inf = 0;
         for (int64_t i = 0; i < V; i++) {
-            if (x[i] != x[i]) { st = ORC_ERR_NAN; break; }
-            if (x[i] == INFINITY) { st = ORC_ERR_POSINF; break; }
+            any_nan |= x[i] != x[i];
+            any_inf |= x[i] == INFINITY;
             if (x[i] > M) M = x[i];
         }
-        if (st != ORC_OK) break;
+        if (any_nan || any_inf) { st = any_nan ? ORC_ERR_NAN : ORC_ERR_POSINF; break; }
         if (M == -INFINITY) { st = ORC_ERR_ALLNEGINF; break; }
         uint64_t S = 0;
         for (int64_t i = 0; i < V; i++) S += fixw(orc_exp(x[i] - M));

@@ -184,6 +184,25 @@ def test_special_values(sv, path):
     assert_same(got, ref)
 
 
+@pytest.mark.parametrize("force", [False, True])
+@pytest.mark.parametrize("path", PATHS)
+def test_error_precedence_and_temperature_overflow(sv, path, force):
+    """A NaN anywhere in the row wins over a +inf before it; a finite score that the
+    temperature (T < 1) takes to +inf is a +inf score, unless the penalty lowers it."""
+    g = np.random.default_rng(10)
+    x = (2 * g.standard_normal((5, 3000))).astype(np.float32)
+    x[0, 9] = np.inf
+    x[0, 2000] = np.nan
+    x[1, 100] = 3.0e38   # / 0.5 overflows
+    x[2, 100] = 3.0e38   # seen: / 3.1 first, then / 0.5 stays finite
+    x[3, 7] = -3.0e38    # seen: * 3.1 gives -inf
+    ids = g.integers(0, 3000, (5, 40))
+    ids[:, 0] = [1, 2, 100, 7, 3]
+    got, ref = run_both(sv, x, g.random(5).astype(np.float32), ids=ids, T=0.5, force=force, path=path)
+    np.testing.assert_array_equal(got["status"], [1, 2, 0, 0, 0])
+    assert_same(got, ref)
+
+
 @pytest.mark.parametrize("path", PATHS)
 def test_history_out_of_range_is_reported(sv, path):
     x = torch.zeros((2, 1000), device=DEV)
