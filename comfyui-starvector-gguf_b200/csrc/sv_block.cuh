@@ -162,20 +162,26 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
-// Bounded wait on an mbarrier phase: gives up after ~1 s of global time.
+__device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(b), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase: gives up after ~1 s of global time (the
+// timer is read only once the phase is found incomplete).
 __device__ inline bool mbar_wait(void* bar, uint32_t phase) {
   const uint32_t b = smem_u32(bar);
+  if (mbar_try(b, phase)) return true;
   const uint64_t t0 = gtimer_ns();
   for (;;) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(b), "r"(phase)
-        : "memory");
-    if (ok) return true;
+    if (mbar_try(b, phase)) return true;
     if (gtimer_ns() - t0 > 1000000000ull) return false;
   }
 }
@@ -453,6 +459,127 @@ __device__ int64_t draw_kept(BlockScratch<NT>& bs, const int* kidx, const float*
   const int64_t token = kidx[bs.flag];
   __syncthreads();
   return token;
+}
+
+// ------------------------------------------------------ finish: one warp
+// The same finish as leader_fast + draw_kept for at most 64 candidates, done by the
+// calling warp alone in registers (no block barriers).
+
+// Ascending bitonic sort of 64 keys in one warp: lane l holds positions l (x0)
+// and 32 + l (x1).
+__device__ __forceinline__ void warp_sort64(uint64_t& x0, uint64_t& x1) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 32) {  // k == 64: partners are the lane's two keys, ascending
+        const uint64_t lo = x0 < x1 ? x0 : x1, hi = x0 < x1 ? x1 : x0;
+        x0 = lo;
+        x1 = hi;
+      } else {
+        const uint64_t p0 = __shfl_xor_sync(0xffffffffu, x0, j);
+        const uint64_t p1 = __shfl_xor_sync(0xffffffffu, x1, j);
+        const bool upper = (lane & j) != 0;
+        // The lower position of an ascending pair (or the upper of a descending
+        // one) keeps the minimum.
+        const bool min0 = ((lane & k) == 0) != upper;
+        const bool min1 = (((32 + lane) & k) == 0) != upper;
+        x0 = min0 ? (x0 < p0 ? x0 : p0) : (x0 < p0 ? p0 : x0);
+        x1 = min1 ? (x1 < p1 ? x1 : p1) : (x1 < p1 ? p1 : x1);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t warp_incl_scan_u64(uint64_t v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+// Value of a per-position register pair (positions l and 32 + l) at position p.
+template <typename T>
+__device__ __forceinline__ T warp_at64(T x0, T x1, int p) {
+  const T a = __shfl_sync(0xffffffffu, x0, p & 31);
+  const T b = __shfl_sync(0xffffffffu, x1, p & 31);
+  return p < 32 ? a : b;
+}
+
+// Top-k threshold with ties (runtime_shared.py:180-181), top-p (:182-186) and the
+// draw for m <= 64 candidates (fv: tempered scores, fi: indices), by the calling
+// warp.  Returns the Kept summary (every lane), sets *token (every lane) and
+// writes the kept list in index order to kidx / kval.
+__device__ inline Kept warp_finish64(const RowArgs& a, const float* fv, const int* fi, int m, float u, int64_t* token,
+                              int* kidx, float* kval) {
+  const int lane = threadIdx.x & 31;
+  const float NEG = Elem<float>::neg_inf();
+  // (a) ascending (value, index) order; padding keys (0) sort first.
+  uint64_t x0 = lane < m ? ((uint64_t)ord_key(fv[lane]) << 32) | (uint32_t)fi[lane] : 0ull;
+  uint64_t x1 = 32 + lane < m ? ((uint64_t)ord_key(fv[32 + lane]) << 32) | (uint32_t)fi[32 + lane] : 0ull;
+  warp_sort64(x0, x1);
+  const int base = 64 - m;
+  const float v0 = key_to_float((uint32_t)(x0 >> 32)), v1 = key_to_float((uint32_t)(x1 >> 32));
+  // (b) k-th largest with ties: kept positions [f0, 64).
+  const float thr = m >= a.kk ? warp_at64(v0, v1, 64 - a.kk) : NEG;
+  const bool in0 = lane >= base && v0 >= thr, in1 = 32 + lane >= base && v1 >= thr;
+  const unsigned b0 = __ballot_sync(0xffffffffu, in0), b1 = __ballot_sync(0xffffffffu, in1);
+  const int f0 = b0 ? __ffs(b0) - 1 : 32 + __ffs(b1) - 1;
+  const float M = __shfl_sync(0xffffffffu, v1, 31);
+  // (c) weights and their ascending prefix sums.
+  const uint64_t w0 = in0 ? fixw(sv_exp(__fsub_rn(v0, M))) : 0ull;
+  const uint64_t w1 = in1 ? fixw(sv_exp(__fsub_rn(v1, M))) : 0ull;
+  const uint64_t P0 = warp_incl_scan_u64(w0);
+  const uint64_t P1 = __shfl_sync(0xffffffffu, P0, 31) + warp_incl_scan_u64(w1);
+  const uint64_t total = __shfl_sync(0xffffffffu, P1, 31);
+  // (d) top-p: the ascending prefix with mass <= floor(total * pthr) goes, never
+  //     the last `keep`.
+  int k0 = f0;
+  uint64_t removed = 0;
+  if (a.pthr > 0.0f) {
+    const uint64_t thrW = mulfloor(total, a.pthr);
+    const unsigned c0 = __ballot_sync(0xffffffffu, in0 && P0 > thrW);
+    const unsigned c1 = __ballot_sync(0xffffffffu, in1 && P1 > thrW);
+    const int rpos = c0 ? __ffs(c0) - 1 : (c1 ? 32 + __ffs(c1) - 1 : 64);
+    int r = rpos - f0;
+    const int cap = (64 - f0) - a.keep > 0 ? (64 - f0) - a.keep : 0;
+    if (r > cap) r = cap;
+    k0 = f0 + r;
+    if (r > 0) removed = warp_at64(P0, P1, k0 - 1);
+  }
+  Kept kp;
+  kp.n = 64 - k0;
+  kp.M = M;
+  kp.tot = total - removed;
+  // (e) the kept entries in index order, then the draw over them.
+  uint64_t y0 = lane >= k0 ? ((uint64_t)(uint32_t)x0 << 8) | (uint32_t)lane : ~0ull;
+  uint64_t y1 = 32 + lane >= k0 ? ((uint64_t)(uint32_t)x1 << 8) | (uint32_t)(32 + lane) : ~0ull;
+  warp_sort64(y0, y1);
+  const int o0 = (int)(y0 & 0xffu) & 63, o1 = (int)(y1 & 0xffu) & 63;
+  const bool q0 = lane < kp.n, q1 = 32 + lane < kp.n;
+  const uint64_t wa = warp_at64(w0, w1, o0), wb = warp_at64(w0, w1, o1);  // every lane shuffles
+  const uint64_t wq0 = q0 ? wa : 0ull, wq1 = q1 ? wb : 0ull;
+  const float vq0 = warp_at64(v0, v1, o0), vq1 = warp_at64(v0, v1, o1);
+  const uint64_t Q0 = warp_incl_scan_u64(wq0);
+  const uint64_t Q1 = __shfl_sync(0xffffffffu, Q0, 31) + warp_incl_scan_u64(wq1);
+  const uint64_t Tu = mulfloor(kp.tot, u);
+  const unsigned h0 = __ballot_sync(0xffffffffu, q0 && Q0 > Tu), h1 = __ballot_sync(0xffffffffu, q1 && Q1 > Tu);
+  const int qd = h0 ? __ffs(h0) - 1 : (h1 ? 32 + __ffs(h1) - 1 : kp.n - 1);
+  *token = (int64_t)(warp_at64(y0, y1, qd) >> 8);
+  if (q0) {
+    kidx[lane] = (int)(y0 >> 8);
+    kval[lane] = vq0;
+  }
+  if (q1) {
+    kidx[32 + lane] = (int)(y1 >> 8);
+    kval[32 + lane] = vq1;
+  }
+  __syncwarp();
+  return kp;
 }
 
 // --------------------------------------------------------- finish: general

@@ -10,21 +10,22 @@
 //   1. the row's seen bitmap in shared memory, from the history;
 //   2. per chunk, one pass over 16-byte units: the unit maximum of the raw scores
 //      is tested against the current lower bound tau of the row's k-th largest
-//      penalised score; only units that pass are re-read element by element, with
-//      the repetition penalty (:172-173), and their elements >= tau appended to the
-//      row's candidates.  The units also feed 128 lane-pair group maxima, a seen
-//      element through a lower bound of its penalised score (group maxima of
-//      disjoint groups are distinct elements, each at or above its group's value,
-//      so their k-th largest bounds the row's k-th largest from below).  In the
+//      penalised score, and the units that reach it are listed.  The units also
+//      feed 128 lane-pair group values, a unit with a seen token through a lower
+//      bound of its penalised maximum (each group value is at or below a distinct
+//      element of its group, so the k-th largest group value bounds the row's
+//      k-th largest from below).  In the
 //      first chunk each warp's r-th largest group maximum (r = ceil(k/8)) gives
 //      the first bound; later group maxima go into a 256-bin histogram over
 //      ordered float keys, whose highest bin edge with at least k maxima at or
 //      above it is a tightening bound;
-//   3. finish: candidates below the final bound are dropped and the rest tempered
-//      (:178-179); then the exact k-th largest with ties (:180-181), top-p over the
-//      ascending (value, index) order with exact fixed-point mass (:182-186) and
-//      the draw from the row's uniform.  A row with too many candidates (huge tie
-//      groups) takes the general path over the whole row.
+//   3. finish: the listed units are read again (from L2) and their elements whose
+//      penalised score (:172-173) reaches the final bound become the candidates,
+//      tempered (:178-179); then the exact k-th largest with ties (:180-181), top-p
+//      over the ascending (value, index) order with exact fixed-point mass
+//      (:182-186) and the draw from the row's uniform, by one warp for up to 64
+//      candidates.  A row with too many (huge tie groups) takes the general path
+//      over the whole row.
 // Status: a NaN anywhere in the row, else a +inf tempered score, else no finite
 // score.  No inter-CTA communication and no scratch memory in global memory.
 #include <cuda_runtime.h>
@@ -44,7 +45,7 @@ constexpr int SCHUNK = 16 * 1024;       // bytes per slot / chunk
 constexpr int SCU = SCHUNK / 16;        // 16-byte units per chunk
 constexpr int UPT = SCU / SNT;          // units per thread per chunk
 constexpr int SBINS = 256;              // bound histogram bins
-constexpr int SCAP = kCandCap;          // candidates per row
+constexpr int UCAP = 2048;              // hit units per row
 constexpr int SFIN = 256;               // candidates the fast finish handles after pruning
 constexpr int kBoundWarp = SWARPS - 1;  // computes the histogram bound after each chunk
 
@@ -52,14 +53,13 @@ struct __align__(16) StreamShared {
   unsigned long long mbar[SBUF];
   BlockScratch<SNT> bs;
   __align__(16) unsigned int bins[SBINS];
-  float wsel[SWARPS];     // first chunk: each warp's r-th largest group maximum
+  float wsel[SWARPS];     // first chunk: each warp's r-th largest group value
   float wtop[SWARPS];     //              and its largest
   float te_pub;           // bound published by the bound warp, read after the next barrier
   unsigned int rmax_key;  // ordered key of the row's largest raw score
-  int cand_n;
+  int unit_n;
   int err;
-  __align__(16) float cand_val[SCAP];  // penalised (not yet tempered) scores
-  int cand_idx[SCAP];
+  __align__(16) int ulist[UCAP];  // hit units; after the prune: finish scratch
   __align__(16) unsigned char work[16 * SFIN];  // finish arrays / general-path scratch
 };
 
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
     }
     if (tid < SBINS / 4) reinterpret_cast<uint4*>(sh.bins)[tid] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
-      sh.cand_n = 0;
+      sh.unit_n = 0;
       sh.te_pub = NEG;
       sh.rmax_key = 0;
     }
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
 #pragma unroll
       for (int j = 0; j < UPT; ++j) {
         const int k = tid + j * SNT;
-        float m = NEG, gv = NEG;
+        float m = NEG;
         if (aligned) {
           sb[j] = k < un ? (bits[((u0 + k) * EPU) >> 5] >> (((u0 + k) * EPU) & 31)) & ((1u << EPU) - 1u) : 0u;
         } else {
@@ -345,21 +345,15 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
           m = v[0];
 #pragma unroll
           for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
-          gv = m;
-          if (sb[j]) {
-            // Seen elements enter the group value through a lower bound of their
-            // penalised score (products rounded down), which needs no division.
-            gv = NEG;
-#pragma unroll
-            for (int e = 0; e < EPU; ++e) {
-              const float lo = v[e] < 0.0f ? __fmul_rd(v[e], rp) : __fmul_rd(v[e], rinv_lo);
-              gv = fmaxf(gv, ((sb[j] >> e) & 1u) ? lo : v[e]);
-            }
-          }
         }
+        // A unit with a seen token enters the group value through a lower bound of
+        // its penalised maximum: the penalty of its raw maximum, with the product
+        // rounded down (no division; the penalty is monotone and never raises a
+        // score).
+        const float lo = __fmul_rd(m, m < 0.0f ? rp : rinv_lo);
         umax[j] = m;
         rmx = max_nan(rmx, m);
-        gsrc = fmaxf(gsrc, gv);  // fmaxf drops NaN; rmx reports it
+        gsrc = fmaxf(gsrc, sb[j] ? lo : m);  // fmaxf drops NaN; rmx reports it
       }
       const float gm = fmaxf(gsrc, __shfl_xor_sync(0xffffffffu, gsrc, 1));  // lane-pair group value
       if (c == 0) {
@@ -394,40 +388,19 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
         while ((span >> bin_shift) >= (uint32_t)SBINS) ++bin_shift;
         te = lower_tau(raw, T);
       }
-      // Candidates: units whose maximum reaches the bound, element by element.
+      // Hit units: their maximum reaches the bound (the raw maximum bounds the
+      // penalised one from above).  The finish tests their elements.
       const float tcmp = fmaxf(te, -3.402823466e38f);  // excludes -inf
       uint32_t hu = 0;
 #pragma unroll
       for (int j = 0; j < UPT; ++j) hu |= (uint32_t)(umax[j] >= tcmp) << j;
       if (hu) {
+        int pos = atomicAdd(&sh.unit_n, __popc(hu));
 #pragma unroll
         for (int j = 0; j < UPT; ++j) {
           if ((hu >> j) & 1u) {
-            const int k = tid + j * SNT;
-            float v[EPU];
-            IO::load(slot, k, v);
-            if (sb[j]) {
-#pragma unroll
-              for (int e = 0; e < EPU; ++e)
-                if ((sb[j] >> e) & 1u) v[e] = penalize(v[e], rp);
-            }
-            uint32_t m = 0;
-#pragma unroll
-            for (int e = 0; e < EPU; ++e) m |= (uint32_t)(v[e] >= tcmp) << e;
-            if (m) {
-              int pos = atomicAdd(&sh.cand_n, __popc(m));
-              const int i0 = (u0 + k) * EPU - g.off_e;
-#pragma unroll
-              for (int e = 0; e < EPU; ++e) {
-                if ((m >> e) & 1u) {
-                  if (pos < SCAP) {
-                    sh.cand_val[pos] = v[e];
-                    sh.cand_idx[pos] = i0 + e;
-                  }
-                  ++pos;
-                }
-              }
-            }
+            if (pos < UCAP) sh.ulist[pos] = u0 + tid + j * SNT;
+            ++pos;
           }
         }
       }
@@ -456,29 +429,51 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
     if (lane == 0 && rmx == rmx) atomicMax(&sh.rmax_key, ord_key(rmx));
     if (tid == 0) bs.flag = 0;
     __syncthreads();
-    const float tfin = fmaxf(te, sh.te_pub);
+    const float tfin = fmaxf(fmaxf(te, sh.te_pub), -3.402823466e38f);  // final bound; excludes -inf
     const float uu = a.uniforms[row];
-    const int n = sh.cand_n;
+    const int nu = sh.unit_n;
     int status = sh.err ? first_err(sh.err) : ST_OK;
-    bool general = status == ST_OK && (a.force_slow || n > SCAP);
+    bool general = status == ST_OK && (a.force_slow || nu > UCAP);
     float* sval = reinterpret_cast<float*>(sh.work);
     int* sidx = reinterpret_cast<int*>(sh.work + 4 * SFIN);
     uint64_t* W = reinterpret_cast<uint64_t*>(sh.work + 8 * SFIN);
     float* fv = reinterpret_cast<float*>(W);
     int* fi = reinterpret_cast<int*>(sh.work + 12 * SFIN);
+    int* kidx = sh.ulist + UCAP / 2;  // kept list (the unit list is consumed by then)
+    float* kval = reinterpret_cast<float*>(sh.ulist);
     int m = 0;
     if (status == ST_OK && !general) {
-      // Drop candidates below the final bound, temper the rest.
+      // The elements of the hit units (read again, from L2) whose penalised score
+      // reaches the final bound, tempered.
       int bad = 0;
-      for (int t = tid; t < n; t += SNT) {
-        const float v = sh.cand_val[t];
-        if (v >= tfin) {
-          const float x = temper(v, T);
-          bad |= x == PINF;
-          const int at = atomicAdd(&bs.flag, 1);
-          if (at < SFIN) {
-            fv[at] = x;
-            fi[at] = sh.cand_idx[t];
+      for (int t = tid; t < nu; t += SNT) {
+        const int uid = sh.ulist[t];
+        const uintptr_t ua = reinterpret_cast<uintptr_t>(g.base16) + (uintptr_t)uid * 16;
+        float v[EPU];
+        if (ua >= g.b_lo && ua + 16 <= g.b_hi) {
+          IO::load(reinterpret_cast<const TIn*>(g.base16), uid, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPU; ++e) {
+            const int64_t i = (int64_t)uid * EPU + e - g.off_e;
+            v[e] = (i >= 0 && i < V) ? Elem<TIn>::load(rowp + i) : NEG;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < EPU; ++e) {
+          if (v[e] >= tfin) {
+            const int i = uid * EPU + e - g.off_e;
+            float x = v[e];
+            if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
+            if (x >= tfin) {
+              const float tx = temper(x, T);
+              bad |= tx == PINF;
+              const int at = atomicAdd(&bs.flag, 1);
+              if (at < SFIN) {
+                fv[at] = tx;
+                fi[at] = i;
+              }
+            }
           }
         }
       }
@@ -511,19 +506,34 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
       __syncthreads();
     }
     if (status == ST_OK && !general) {
-      kept = leader_fast<SNT>(a, bs, fv, fi, m, sval, sidx, W, reinterpret_cast<uint64_t*>(sh.cand_val),
-                              sh.cand_idx, sh.cand_val);
-      token = draw_kept<SNT>(bs, sh.cand_idx, sh.cand_val, kept, uu, reinterpret_cast<uint64_t*>(sh.work));
+      if (m <= 64) {
+        // Few candidates: one warp finishes in registers.
+        if (warp == 0) {
+          kept = warp_finish64(a, fv, fi, m, uu, &token, kidx, kval);
+          if (lane == 0) {
+            bs.flag2 = kept.n;
+            bs.fval = kept.M;
+            bs.u64a = kept.tot;
+          }
+        }
+        __syncthreads();
+        kept.n = bs.flag2;
+        kept.M = bs.fval;
+        kept.tot = bs.u64a;
+      } else {
+        kept = leader_fast<SNT>(a, bs, fv, fi, m, sval, sidx, W, reinterpret_cast<uint64_t*>(sh.ulist), kidx, kval);
+        token = draw_kept<SNT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(sh.work));
+      }
       const float Sf = fix_to_float(kept.tot);
       for (int j = tid; j < kept.n; j += SNT) {
-        const float p = __fdiv_rn(sv_exp(__fsub_rn(sh.cand_val[j], kept.M)), Sf);
+        const float p = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kept.M)), Sf);
         if (j < a.out_cap) {
-          if (a.out_idx) a.out_idx[row * a.out_cap + j] = sh.cand_idx[j];
+          if (a.out_idx) a.out_idx[row * a.out_cap + j] = kidx[j];
           if (a.out_prob) a.out_prob[row * a.out_cap + j] = p;
-          if (a.out_score) a.out_score[row * a.out_cap + j] = sh.cand_val[j];
+          if (a.out_score) a.out_score[row * a.out_cap + j] = kval[j];
         }
         if (a.out_dense && a.dense_mode != DENSE_NONE)
-          a.out_dense[row * a.dense_stride + sh.cand_idx[j]] = a.dense_mode == DENSE_SCORES ? sh.cand_val[j] : p;
+          a.out_dense[row * a.dense_stride + kidx[j]] = a.dense_mode == DENSE_SCORES ? kval[j] : p;
       }
     } else if (general) {
       auto seen = [&](int64_t i) -> bool { return (bits[i >> 5] >> (i & 31)) & 1u; };
