@@ -462,31 +462,39 @@ __device__ int64_t draw_kept(BlockScratch<NT>& bs, const int* kidx, const float*
 }
 
 // ------------------------------------------------------ finish: one warp
-// The same finish as leader_fast + draw_kept for at most 64 candidates, done by the
-// calling warp alone in registers (no block barriers).
+// The same finish as leader_fast + draw_kept for at most 32 * N candidates, done
+// by the calling warp alone in registers (no block barriers).  Lane l holds the
+// positions s * 32 + l, s < N.
 
-// Ascending bitonic sort of 64 keys in one warp: lane l holds positions l (x0)
-// and 32 + l (x1).
-__device__ __forceinline__ void warp_sort64(uint64_t& x0, uint64_t& x1) {
+// Ascending bitonic sort of 32 * N keys in one warp.
+template <int N>
+__device__ __forceinline__ void warp_sort(uint64_t (&x)[N]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int k = 2; k <= 64; k <<= 1) {
+  for (int k = 2; k <= 32 * N; k <<= 1) {
 #pragma unroll
     for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j == 32) {  // k == 64: partners are the lane's two keys, ascending
-        const uint64_t lo = x0 < x1 ? x0 : x1, hi = x0 < x1 ? x1 : x0;
-        x0 = lo;
-        x1 = hi;
+      if (j >= 32) {  // partners in the same lane: registers s and s | (j / 32)
+#pragma unroll
+        for (int s = 0; s < N; ++s) {
+          if ((s & (j >> 5)) == 0) {
+            const int t = s | (j >> 5);
+            const bool asc = ((s * 32) & k) == 0;
+            const uint64_t lo = x[s] < x[t] ? x[s] : x[t], hi = x[s] < x[t] ? x[t] : x[s];
+            x[s] = asc ? lo : hi;
+            x[t] = asc ? hi : lo;
+          }
+        }
       } else {
-        const uint64_t p0 = __shfl_xor_sync(0xffffffffu, x0, j);
-        const uint64_t p1 = __shfl_xor_sync(0xffffffffu, x1, j);
         const bool upper = (lane & j) != 0;
-        // The lower position of an ascending pair (or the upper of a descending
-        // one) keeps the minimum.
-        const bool min0 = ((lane & k) == 0) != upper;
-        const bool min1 = (((32 + lane) & k) == 0) != upper;
-        x0 = min0 ? (x0 < p0 ? x0 : p0) : (x0 < p0 ? p0 : x0);
-        x1 = min1 ? (x1 < p1 ? x1 : p1) : (x1 < p1 ? p1 : x1);
+#pragma unroll
+        for (int s = 0; s < N; ++s) {
+          const uint64_t p = __shfl_xor_sync(0xffffffffu, x[s], j);
+          // The lower position of an ascending pair (or the upper of a descending
+          // one) keeps the minimum.
+          const bool keep_min = (((s * 32 + lane) & k) == 0) != upper;
+          x[s] = keep_min ? (x[s] < p ? x[s] : p) : (x[s] < p ? p : x[s]);
+        }
       }
     }
   }
@@ -502,82 +510,114 @@ __device__ __forceinline__ uint64_t warp_incl_scan_u64(uint64_t v) {
   return v;
 }
 
-// Value of a per-position register pair (positions l and 32 + l) at position p.
-template <typename T>
-__device__ __forceinline__ T warp_at64(T x0, T x1, int p) {
-  const T a = __shfl_sync(0xffffffffu, x0, p & 31);
-  const T b = __shfl_sync(0xffffffffu, x1, p & 31);
-  return p < 32 ? a : b;
+// The value at position p (per lane) of a per-position register set.  Every lane
+// must call it.
+template <int N, typename T>
+__device__ __forceinline__ T warp_at(const T (&x)[N], int p) {
+  T r = x[0];
+#pragma unroll
+  for (int s = 0; s < N; ++s) {
+    const T t = __shfl_sync(0xffffffffu, x[s], p & 31);
+    if ((p >> 5) == s) r = t;
+  }
+  return r;
+}
+
+// First position (s * 32 + lane order) whose predicate holds, or `none`.
+template <int N>
+__device__ __forceinline__ int warp_first(const bool (&pr)[N], int none) {
+#pragma unroll
+  for (int s = 0; s < N; ++s) {
+    const unsigned b = __ballot_sync(0xffffffffu, pr[s]);
+    if (b) return s * 32 + __ffs(b) - 1;
+  }
+  return none;
 }
 
 // Top-k threshold with ties (runtime_shared.py:180-181), top-p (:182-186) and the
-// draw for m <= 64 candidates (fv: tempered scores, fi: indices), by the calling
-// warp.  Returns the Kept summary (every lane), sets *token (every lane) and
-// writes the kept list in index order to kidx / kval.
-__device__ inline Kept warp_finish64(const RowArgs& a, const float* fv, const int* fi, int m, float u, int64_t* token,
-                              int* kidx, float* kval) {
+// draw for m <= 32 * N candidates (fv: tempered scores, fi: indices; m >= 1), by
+// the calling warp.  Returns the Kept summary (every lane), sets *token (every
+// lane) and writes the kept list in index order to kidx / kval.
+template <int N>
+__device__ Kept warp_finish(const RowArgs& a, const float* fv, const int* fi, int m, float u, int64_t* token,
+                            int* kidx, float* kval) {
+  constexpr int C = 32 * N;
   const int lane = threadIdx.x & 31;
   const float NEG = Elem<float>::neg_inf();
   // (a) ascending (value, index) order; padding keys (0) sort first.
-  uint64_t x0 = lane < m ? ((uint64_t)ord_key(fv[lane]) << 32) | (uint32_t)fi[lane] : 0ull;
-  uint64_t x1 = 32 + lane < m ? ((uint64_t)ord_key(fv[32 + lane]) << 32) | (uint32_t)fi[32 + lane] : 0ull;
-  warp_sort64(x0, x1);
-  const int base = 64 - m;
-  const float v0 = key_to_float((uint32_t)(x0 >> 32)), v1 = key_to_float((uint32_t)(x1 >> 32));
-  // (b) k-th largest with ties: kept positions [f0, 64).
-  const float thr = m >= a.kk ? warp_at64(v0, v1, 64 - a.kk) : NEG;
-  const bool in0 = lane >= base && v0 >= thr, in1 = 32 + lane >= base && v1 >= thr;
-  const unsigned b0 = __ballot_sync(0xffffffffu, in0), b1 = __ballot_sync(0xffffffffu, in1);
-  const int f0 = b0 ? __ffs(b0) - 1 : 32 + __ffs(b1) - 1;
-  const float M = __shfl_sync(0xffffffffu, v1, 31);
+  uint64_t x[N];
+#pragma unroll
+  for (int s = 0; s < N; ++s) {
+    const int p = s * 32 + lane;
+    x[s] = p < m ? ((uint64_t)ord_key(fv[p]) << 32) | (uint32_t)fi[p] : 0ull;
+  }
+  warp_sort<N>(x);
+  float v[N];
+#pragma unroll
+  for (int s = 0; s < N; ++s) v[s] = key_to_float((uint32_t)(x[s] >> 32));
+  // (b) k-th largest with ties: kept positions [f0, C).
+  const float thr = m >= a.kk ? warp_at<N>(v, C - a.kk) : NEG;
+  bool in[N];
+#pragma unroll
+  for (int s = 0; s < N; ++s) in[s] = s * 32 + lane >= C - m && v[s] >= thr;
+  const int f0 = warp_first<N>(in, C - 1);
+  const float M = __shfl_sync(0xffffffffu, v[N - 1], 31);
   // (c) weights and their ascending prefix sums.
-  const uint64_t w0 = in0 ? fixw(sv_exp(__fsub_rn(v0, M))) : 0ull;
-  const uint64_t w1 = in1 ? fixw(sv_exp(__fsub_rn(v1, M))) : 0ull;
-  const uint64_t P0 = warp_incl_scan_u64(w0);
-  const uint64_t P1 = __shfl_sync(0xffffffffu, P0, 31) + warp_incl_scan_u64(w1);
-  const uint64_t total = __shfl_sync(0xffffffffu, P1, 31);
+  uint64_t w[N], P[N], carry = 0;
+#pragma unroll
+  for (int s = 0; s < N; ++s) {
+    w[s] = in[s] ? fixw(sv_exp(__fsub_rn(v[s], M))) : 0ull;
+    P[s] = carry + warp_incl_scan_u64(w[s]);
+    carry = __shfl_sync(0xffffffffu, P[s], 31);
+  }
+  const uint64_t total = carry;
   // (d) top-p: the ascending prefix with mass <= floor(total * pthr) goes, never
   //     the last `keep`.
   int k0 = f0;
   uint64_t removed = 0;
   if (a.pthr > 0.0f) {
     const uint64_t thrW = mulfloor(total, a.pthr);
-    const unsigned c0 = __ballot_sync(0xffffffffu, in0 && P0 > thrW);
-    const unsigned c1 = __ballot_sync(0xffffffffu, in1 && P1 > thrW);
-    const int rpos = c0 ? __ffs(c0) - 1 : (c1 ? 32 + __ffs(c1) - 1 : 64);
-    int r = rpos - f0;
-    const int cap = (64 - f0) - a.keep > 0 ? (64 - f0) - a.keep : 0;
+    bool c[N];
+#pragma unroll
+    for (int s = 0; s < N; ++s) c[s] = in[s] && P[s] > thrW;
+    int r = warp_first<N>(c, C) - f0;
+    const int cap = (C - f0) - a.keep > 0 ? (C - f0) - a.keep : 0;
     if (r > cap) r = cap;
     k0 = f0 + r;
-    if (r > 0) removed = warp_at64(P0, P1, k0 - 1);
+    if (r > 0) removed = warp_at<N>(P, k0 - 1);
   }
   Kept kp;
-  kp.n = 64 - k0;
+  kp.n = C - k0;
   kp.M = M;
   kp.tot = total - removed;
   // (e) the kept entries in index order, then the draw over them.
-  uint64_t y0 = lane >= k0 ? ((uint64_t)(uint32_t)x0 << 8) | (uint32_t)lane : ~0ull;
-  uint64_t y1 = 32 + lane >= k0 ? ((uint64_t)(uint32_t)x1 << 8) | (uint32_t)(32 + lane) : ~0ull;
-  warp_sort64(y0, y1);
-  const int o0 = (int)(y0 & 0xffu) & 63, o1 = (int)(y1 & 0xffu) & 63;
-  const bool q0 = lane < kp.n, q1 = 32 + lane < kp.n;
-  const uint64_t wa = warp_at64(w0, w1, o0), wb = warp_at64(w0, w1, o1);  // every lane shuffles
-  const uint64_t wq0 = q0 ? wa : 0ull, wq1 = q1 ? wb : 0ull;
-  const float vq0 = warp_at64(v0, v1, o0), vq1 = warp_at64(v0, v1, o1);
-  const uint64_t Q0 = warp_incl_scan_u64(wq0);
-  const uint64_t Q1 = __shfl_sync(0xffffffffu, Q0, 31) + warp_incl_scan_u64(wq1);
+  uint64_t y[N];
+#pragma unroll
+  for (int s = 0; s < N; ++s) {
+    const int p = s * 32 + lane;
+    y[s] = p >= k0 ? ((uint64_t)(uint32_t)x[s] << 8) | (uint32_t)p : ~0ull;
+  }
+  warp_sort<N>(y);
+  uint64_t Q[N];
+  bool hit[N];
   const uint64_t Tu = mulfloor(kp.tot, u);
-  const unsigned h0 = __ballot_sync(0xffffffffu, q0 && Q0 > Tu), h1 = __ballot_sync(0xffffffffu, q1 && Q1 > Tu);
-  const int qd = h0 ? __ffs(h0) - 1 : (h1 ? 32 + __ffs(h1) - 1 : kp.n - 1);
-  *token = (int64_t)(warp_at64(y0, y1, qd) >> 8);
-  if (q0) {
-    kidx[lane] = (int)(y0 >> 8);
-    kval[lane] = vq0;
+  carry = 0;
+#pragma unroll
+  for (int s = 0; s < N; ++s) {
+    const int q = s * 32 + lane;
+    const int o = (int)(y[s] & 0xffu) & (C - 1);
+    const uint64_t wq = warp_at<N>(w, o);  // every lane shuffles
+    const float vq = warp_at<N>(v, o);
+    Q[s] = carry + warp_incl_scan_u64(q < kp.n ? wq : 0ull);
+    carry = __shfl_sync(0xffffffffu, Q[s], 31);
+    hit[s] = q < kp.n && Q[s] > Tu;
+    if (q < kp.n) {
+      kidx[q] = (int)(y[s] >> 8);
+      kval[q] = vq;
+    }
   }
-  if (q1) {
-    kidx[32 + lane] = (int)(y1 >> 8);
-    kval[32 + lane] = vq1;
-  }
+  const int qd = warp_first<N>(hit, kp.n - 1);
+  *token = (int64_t)(warp_at<N>(y, qd) >> 8);
   __syncwarp();
   return kp;
 }

@@ -10,22 +10,21 @@
 //   1. the row's seen bitmap in shared memory, from the history;
 //   2. per chunk, one pass over 16-byte units: the unit maximum of the raw scores
 //      is tested against the current lower bound tau of the row's k-th largest
-//      penalised score, and the units that reach it are listed.  The units also
-//      feed 128 lane-pair group values, a unit with a seen token through a lower
-//      bound of its penalised maximum (each group value is at or below a distinct
-//      element of its group, so the k-th largest group value bounds the row's
-//      k-th largest from below).  In the
-//      first chunk each warp's r-th largest group maximum (r = ceil(k/8)) gives
-//      the first bound; later group maxima go into a 256-bin histogram over
-//      ordered float keys, whose highest bin edge with at least k maxima at or
-//      above it is a tightening bound;
-//   3. finish: the listed units are read again (from L2) and their elements whose
-//      penalised score (:172-173) reaches the final bound become the candidates,
-//      tempered (:178-179); then the exact k-th largest with ties (:180-181), top-p
-//      over the ascending (value, index) order with exact fixed-point mass
-//      (:182-186) and the draw from the row's uniform, by one warp for up to 64
-//      candidates.  A row with too many (huge tie groups) takes the general path
-//      over the whole row.
+//      penalised score, and the units that reach it are kept (their 16 bytes and
+//      seen bits).  The units also feed 128 lane-pair group values, a unit with a
+//      seen token through a lower bound of its penalised maximum (each group value
+//      is at or below a distinct element of its group, so the k-th largest group
+//      value bounds the row's k-th largest from below).  In the first chunk the
+//      exact k-th largest of the chunk's group values gives the first bound;
+//      later group values go into a 256-bin histogram over ordered float keys,
+//      whose highest bin edge with at least k values at or above it is a
+//      tightening bound;
+//   3. finish: the kept units' elements whose penalised score (:172-173) reaches
+//      the final bound are the candidates, tempered (:178-179); then the exact
+//      k-th largest with ties (:180-181), top-p over the ascending (value, index)
+//      order with exact fixed-point mass (:182-186) and the draw from the row's
+//      uniform, by one warp for up to 64 candidates.  A row with too many (huge tie
+//      groups) takes the general path over the whole row.
 // Status: a NaN anywhere in the row, else a +inf tempered score, else no finite
 // score.  No inter-CTA communication and no scratch memory in global memory.
 #include <cuda_runtime.h>
@@ -45,7 +44,7 @@ constexpr int SCHUNK = 16 * 1024;       // bytes per slot / chunk
 constexpr int SCU = SCHUNK / 16;        // 16-byte units per chunk
 constexpr int UPT = SCU / SNT;          // units per thread per chunk
 constexpr int SBINS = 256;              // bound histogram bins
-constexpr int UCAP = 2048;              // hit units per row
+constexpr int UCAP = 704;               // hit units per row (their 16 bytes are kept)
 constexpr int SFIN = 256;               // candidates the fast finish handles after pruning
 constexpr int kBoundWarp = SWARPS - 1;  // computes the histogram bound after each chunk
 
@@ -53,13 +52,14 @@ struct __align__(16) StreamShared {
   unsigned long long mbar[SBUF];
   BlockScratch<SNT> bs;
   __align__(16) unsigned int bins[SBINS];
-  float wsel[SWARPS];     // first chunk: each warp's r-th largest group value
-  float wtop[SWARPS];     //              and its largest
+  float gsort[SWARPS][16];  // first chunk: each warp's group values, descending
+  float first_raw;          //              and their kk-th largest
   float te_pub;           // bound published by the bound warp, read after the next barrier
   unsigned int rmax_key;  // ordered key of the row's largest raw score
   int unit_n;
   int err;
-  __align__(16) int ulist[UCAP];  // hit units; after the prune: finish scratch
+  __align__(16) uint4 udata[UCAP];  // hit units' 16 bytes; after the prune: finish scratch
+  int uidx[UCAP];                   // hit units: (unit << 8) | seen bits
   __align__(16) unsigned char work[16 * SFIN];  // finish arrays / general-path scratch
 };
 
@@ -357,9 +357,10 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
       }
       const float gm = fmaxf(gsrc, __shfl_xor_sync(0xffffffffu, gsrc, 1));  // lane-pair group value
       if (c == 0) {
-        // First bound: each warp's r-th largest of its 16 group values (ties by
-        // group), r = ceil(kk / 8): 8r >= kk distinct elements lie at or above the
-        // smallest of them.
+        // First bound: the exact kk-th largest of the chunk's 128 group values in
+        // the order (value desc, warp, group).  Each warp sorts its 16 by rank; a
+        // value's global rank adds its position in the other warps' lists (binary
+        // search); the value of rank kk - 1 is the bound.
         const int pair = lane >> 1;
         int rank = 0;
 #pragma unroll
@@ -367,21 +368,29 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
           const float w = __shfl_sync(0xffffffffu, gm, 2 * q);
           rank += (w > gm) || (w == gm && q < pair);
         }
-        const unsigned sel = __ballot_sync(0xffffffffu, rank == ((kk + 7) >> 3) - 1);
-        const unsigned top = __ballot_sync(0xffffffffu, rank == 0);
-        const float wsel = __shfl_sync(0xffffffffu, gm, __ffs(sel) - 1);
-        const float wtop = __shfl_sync(0xffffffffu, gm, __ffs(top) - 1);
-        if (lane == 0) {
-          sh.wsel[warp] = wsel;
-          sh.wtop[warp] = wtop;
-        }
+        if ((lane & 1) == 0) sh.gsort[warp][rank] = gm;
         __syncthreads();
-        float raw = sh.wsel[0], hi = sh.wtop[0];
 #pragma unroll
-        for (int w = 1; w < SWARPS; ++w) {
-          raw = fminf(raw, sh.wsel[w]);
-          hi = fmaxf(hi, sh.wtop[w]);
+        for (int w = 0; w < SWARPS; ++w) {
+          if (w == warp) continue;
+          int lo = 0, hi = 16;  // entries of warp w that come before this value
+#pragma unroll
+          for (int it = 0; it < 5; ++it) {
+            if (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              const float e = sh.gsort[w][mid];
+              if (e > gm || (e == gm && w < warp)) lo = mid + 1;
+              else hi = mid;
+            }
+          }
+          rank += lo;
         }
+        if ((lane & 1) == 0 && rank == kk - 1) sh.first_raw = gm;
+        __syncthreads();
+        const float raw = sh.first_raw;
+        float hi = sh.gsort[0][0];
+#pragma unroll
+        for (int w = 1; w < SWARPS; ++w) hi = fmaxf(hi, sh.gsort[w][0]);
         base_key = ord_key(raw);
         const uint32_t span = ord_key(hi) > base_key ? ord_key(hi) - base_key : 0u;
         bin_shift = 0;
@@ -389,7 +398,8 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
         te = lower_tau(raw, T);
       }
       // Hit units: their maximum reaches the bound (the raw maximum bounds the
-      // penalised one from above).  The finish tests their elements.
+      // penalised one from above).  Their 16 bytes and seen bits are kept for the
+      // finish, which tests their elements.
       const float tcmp = fmaxf(te, -3.402823466e38f);  // excludes -inf
       uint32_t hu = 0;
 #pragma unroll
@@ -399,7 +409,11 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
 #pragma unroll
         for (int j = 0; j < UPT; ++j) {
           if ((hu >> j) & 1u) {
-            if (pos < UCAP) sh.ulist[pos] = u0 + tid + j * SNT;
+            if (pos < UCAP) {
+              const int k = tid + j * SNT;
+              sh.udata[pos] = reinterpret_cast<const uint4*>(slot)[k];
+              sh.uidx[pos] = ((u0 + k) << 8) | (int)sb[j];
+            }
             ++pos;
           }
         }
@@ -439,32 +453,25 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
     uint64_t* W = reinterpret_cast<uint64_t*>(sh.work + 8 * SFIN);
     float* fv = reinterpret_cast<float*>(W);
     int* fi = reinterpret_cast<int*>(sh.work + 12 * SFIN);
-    int* kidx = sh.ulist + UCAP / 2;  // kept list (the unit list is consumed by then)
-    float* kval = reinterpret_cast<float*>(sh.ulist);
+    // Kept list and leader_fast's key array, in the unit data (consumed by then).
+    int* kidx = reinterpret_cast<int*>(sh.udata) + 2 * SFIN;
+    float* kval = reinterpret_cast<float*>(sh.udata);
     int m = 0;
     if (status == ST_OK && !general) {
-      // The elements of the hit units (read again, from L2) whose penalised score
-      // reaches the final bound, tempered.
+      // The elements of the hit units whose penalised score reaches the final
+      // bound, tempered (elements outside the row were staged as -inf).
       int bad = 0;
       for (int t = tid; t < nu; t += SNT) {
-        const int uid = sh.ulist[t];
-        const uintptr_t ua = reinterpret_cast<uintptr_t>(g.base16) + (uintptr_t)uid * 16;
+        const int ent = sh.uidx[t];
+        const int uid = ent >> 8;
         float v[EPU];
-        if (ua >= g.b_lo && ua + 16 <= g.b_hi) {
-          IO::load(reinterpret_cast<const TIn*>(g.base16), uid, v);
-        } else {
-#pragma unroll
-          for (int e = 0; e < EPU; ++e) {
-            const int64_t i = (int64_t)uid * EPU + e - g.off_e;
-            v[e] = (i >= 0 && i < V) ? Elem<TIn>::load(rowp + i) : NEG;
-          }
-        }
+        IO::load(reinterpret_cast<const TIn*>(sh.udata), t, v);
 #pragma unroll
         for (int e = 0; e < EPU; ++e) {
           if (v[e] >= tfin) {
             const int i = uid * EPU + e - g.off_e;
             float x = v[e];
-            if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
+            if ((ent >> e) & 1) x = penalize(x, rp);
             if (x >= tfin) {
               const float tx = temper(x, T);
               bad |= tx == PINF;
@@ -509,7 +516,7 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
       if (m <= 64) {
         // Few candidates: one warp finishes in registers.
         if (warp == 0) {
-          kept = warp_finish64(a, fv, fi, m, uu, &token, kidx, kval);
+          kept = warp_finish<2>(a, fv, fi, m, uu, &token, kidx, kval);
           if (lane == 0) {
             bs.flag2 = kept.n;
             bs.fval = kept.M;
@@ -521,7 +528,7 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
         kept.M = bs.fval;
         kept.tot = bs.u64a;
       } else {
-        kept = leader_fast<SNT>(a, bs, fv, fi, m, sval, sidx, W, reinterpret_cast<uint64_t*>(sh.ulist), kidx, kval);
+        kept = leader_fast<SNT>(a, bs, fv, fi, m, sval, sidx, W, reinterpret_cast<uint64_t*>(sh.udata), kidx, kval);
         token = draw_kept<SNT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(sh.work));
       }
       const float Sf = fix_to_float(kept.tot);
