@@ -162,14 +162,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
+// One try_wait; the thread may be suspended up to ~1 ms (it resumes as soon as the
+// phase completes), so a waiting warp issues few instructions.
 __device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t phase) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(b), "r"(phase)
+      : "r"(b), "r"(phase), "r"(1000000u)
       : "memory");
   return ok != 0;
 }

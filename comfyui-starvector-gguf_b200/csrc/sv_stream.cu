@@ -1,6 +1,6 @@
 // sv_stream.cu -- the streaming row kernel (sm_100a): many independent rows.
 //
-// Persistent CTAs (three per SM) work through their rows one at a time.  A row's
+// Persistent CTAs work through their rows one at a time.  A row's
 // logits (and, ahead of them, its history ids) stream through a per-CTA ring of
 // shared-memory slots filled by TMA bulk copies (cp.async.bulk, one mbarrier per
 // slot); the ring runs ahead across row boundaries, so HBM keeps streaming while
@@ -37,9 +37,16 @@ namespace sv {
 
 namespace {
 
-constexpr int SNT = 256;                // threads per CTA
+// Resident CTAs per SM: 3 (256 threads, a 3-slot ring each) or 1 (512 threads, a
+// 12-slot ring).
+#ifndef SV_STREAM_CTAS_PER_SM
+#define SV_STREAM_CTAS_PER_SM 3
+#endif
+constexpr int kCtasPerSm = SV_STREAM_CTAS_PER_SM;
+constexpr int SNT = kCtasPerSm == 1 ? 512 : 256;  // threads per CTA
 constexpr int SWARPS = SNT / 32;
-constexpr int SBUF = 3;                 // ring slots
+constexpr int SBUF = kCtasPerSm == 1 ? 12 : 3;  // ring slots
+constexpr size_t kSmemCap = kCtasPerSm == 1 ? 227 * 1024 : 74 * 1024;  // per CTA
 constexpr int SCHUNK = 16 * 1024;       // bytes per slot / chunk
 constexpr int SCU = SCHUNK / 16;        // 16-byte units per chunk
 constexpr int UPT = SCU / SNT;          // units per thread per chunk
@@ -180,7 +187,7 @@ __device__ __forceinline__ int mark_staged(const unsigned char* src, int64_t L, 
 }
 
 template <typename TIn>
-__global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
+__global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   StreamShared& sh = *reinterpret_cast<StreamShared*>(smem_raw);
   BlockScratch<SNT>& bs = sh.bs;
@@ -325,35 +332,52 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
           }
         }
       }
-      // Unit maxima, seen bits and this lane's group value.  For aligned rows this
-      // thread's units sit at a fixed bit offset in consecutive bitmap words.
+      // Unit maxima, seen bits and this lane's group value.  A unit with a seen
+      // token enters the group value through a lower bound of its penalised
+      // maximum: the penalty of its raw maximum, with the product rounded down (no
+      // division; the penalty is monotone and never raises a score).  Full chunks
+      // of aligned rows (the common case) take a path without bounds checks, their
+      // units at a fixed bit offset in consecutive bitmap words.
       float umax[UPT];
       uint32_t sb[UPT];
       float gsrc = NEG;
-#pragma unroll
-      for (int j = 0; j < UPT; ++j) {
-        const int k = tid + j * SNT;
-        float m = NEG;
-        if (aligned) {
-          sb[j] = k < un ? (bits[((u0 + k) * EPU) >> 5] >> (((u0 + k) * EPU) & 31)) & ((1u << EPU) - 1u) : 0u;
-        } else {
-          sb[j] = k < un ? unit_bits(bits, (int64_t)(u0 + k) * EPU - g.off_e, EPU, V) : 0u;
-        }
-        if (k < un) {
-          float v[EPU];
-          IO::load(slot, k, v);
-          m = v[0];
-#pragma unroll
-          for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
-        }
-        // A unit with a seen token enters the group value through a lower bound of
-        // its penalised maximum: the penalty of its raw maximum, with the product
-        // rounded down (no division; the penalty is monotone and never raises a
-        // score).
+      auto unit = [&](int j, float m, uint32_t bitsj) {
         const float lo = __fmul_rd(m, m < 0.0f ? rp : rinv_lo);
         umax[j] = m;
+        sb[j] = bitsj;
         rmx = max_nan(rmx, m);
-        gsrc = fmaxf(gsrc, sb[j] ? lo : m);  // fmaxf drops NaN; rmx reports it
+        gsrc = fmaxf(gsrc, bitsj ? lo : m);  // fmaxf drops NaN; rmx reports it
+      };
+      if (aligned && un == SCU) {
+        const int e0 = (u0 + tid) * EPU;
+        const uint32_t* bw = bits + (e0 >> 5);
+        const int shf = e0 & 31;
+#pragma unroll
+        for (int j = 0; j < UPT; ++j) {
+          float v[EPU];
+          IO::load(slot, tid + j * SNT, v);
+          float m = v[0];
+#pragma unroll
+          for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
+          unit(j, m, (bw[j * (SNT * EPU / 32)] >> shf) & ((1u << EPU) - 1u));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < UPT; ++j) {
+          const int k = tid + j * SNT;
+          float m = NEG;
+          uint32_t b = 0;
+          if (k < un) {
+            b = aligned ? (bits[((u0 + k) * EPU) >> 5] >> (((u0 + k) * EPU) & 31)) & ((1u << EPU) - 1u)
+                        : unit_bits(bits, (int64_t)(u0 + k) * EPU - g.off_e, EPU, V);
+            float v[EPU];
+            IO::load(slot, k, v);
+            m = v[0];
+#pragma unroll
+            for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
+          }
+          unit(j, m, b);
+        }
       }
       const float gm = fmaxf(gsrc, __shfl_xor_sync(0xffffffffu, gsrc, 1));  // lane-pair group value
       if (c == 0) {
@@ -424,16 +448,22 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
         if (gm >= te && k >= base_key)
           atomicAdd(&sh.bins[min((uint32_t)(SBINS - 1), (k - base_key) >> bin_shift)], 1u);
       }
-      __syncthreads();  // the slot is consumed; the bins hold this chunk's values
-      // The bound published during the previous chunk; the bound warp then publishes
-      // one from the bins complete up to this chunk.  (A thread may read either: both
-      // are valid bounds.)
-      te = fmaxf(te, sh.te_pub);
+      // The bound warp publishes a bound from the bins as they stand, before the
+      // barrier so that its latency overlaps the other warps' passes (counts only
+      // grow, so a partial histogram gives a valid, lower bound).
       if (warp == kBoundWarp) {
+        __syncwarp();
         const float tb = hist_bound(sh.bins, base_key, bin_shift, kk, T);
-        if (lane == 0) sh.te_pub = tb;
+        if (lane == 0) sh.te_pub = fmaxf(sh.te_pub, tb);
       }
+      __syncthreads();  // the slot is consumed
+      te = fmaxf(te, sh.te_pub);
       if (tid == 0) issue_next();
+    }
+    // The final bound, from the complete bins.
+    if (warp == kBoundWarp) {
+      const float tb = hist_bound(sh.bins, base_key, bin_shift, kk, T);
+      if (lane == 0) sh.te_pub = fmaxf(sh.te_pub, tb);
     }
 
     // 3. finish the row.
@@ -505,6 +535,28 @@ __global__ void __launch_bounds__(SNT, 3) stream_kernel(const RowArgs a) {
       }
     }
     if (status == ST_OK && !general && m == 0) status = ST_ALLNEGINF;
+    if (status == ST_OK && !general && m <= 64 && !(a.out_dense && a.dense_mode != DENSE_NONE)) {
+      // Common case: warp 0 finishes the row in registers while the other warps
+      // start the next one (it touches nothing the next row's start uses).
+      if (warp == 0) {
+        int64_t tok = -1;
+        const Kept kp = warp_finish<2>(a, fv, fi, m, uu, &tok, kidx, kval);
+        const float Sf = fix_to_float(kp.tot);
+        for (int j = lane; j < kp.n && j < a.out_cap; j += 32) {
+          if (a.out_idx) a.out_idx[row * a.out_cap + j] = kidx[j];
+          if (a.out_prob) a.out_prob[row * a.out_cap + j] = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kp.M)), Sf);
+          if (a.out_score) a.out_score[row * a.out_cap + j] = kval[j];
+        }
+        if (lane == 0) {
+          a.out_token[row] = tok;
+          if (a.out_count) a.out_count[row] = kp.n;
+          if (a.out_status) a.out_status[row] = ST_OK;
+          if (a.seen_bits && tok >= 0) atomicOr(&a.seen_bits[row * a.seen_bits_stride + (tok >> 5)], 1u << (tok & 31));
+          sh.err = 0;
+        }
+      }
+      continue;
+    }
     Kept kept = {0, 0.0f, 0};
     int64_t token = -1;
     if (a.out_dense && a.dense_mode != DENSE_NONE && status == ST_OK && !general) {
@@ -584,7 +636,7 @@ cudaError_t launch_stream_t(const RowArgs& a, size_t smem, cudaStream_t stream) 
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    slots[dev] = 3 * sms;
+    slots[dev] = kCtasPerSm * sms;
     configured[dev] = 1;
   }
   const int grid = a.rows < slots[dev] ? a.rows : slots[dev];
@@ -595,10 +647,10 @@ cudaError_t launch_stream_t(const RowArgs& a, size_t smem, cudaStream_t stream) 
 }  // namespace
 
 // Dynamic shared memory of the streaming kernel for a vocabulary, or 0 when it
-// would not leave room for three CTAs per SM.
+// would not leave room for its CTAs per SM.
 size_t stream_smem_bytes(int64_t vocab) {
   const size_t s = kStaticBytes + (size_t)SBUF * SCHUNK + bitmap_bytes(vocab);
-  return s <= 74 * 1024 ? s : 0;
+  return s <= kSmemCap ? s : 0;
 }
 
 cudaError_t launch_stream(const RowArgs& a, size_t smem, cudaStream_t stream) {
