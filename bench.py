@@ -197,6 +197,19 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+def profiled_traffic():
+    """DRAM bytes (read + write) of one stream-kernel launch on this workload, from
+    the committed ncu summary (profiles/stream_kernel_cfg4.md), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "stream_kernel_cfg4.md")) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return int(line.split(":")[1])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
 def cpu_port_rows_per_s(data, seconds=10.0, chunk=64):
     """The CPU port of the reference algorithm (oracle/) on all host threads, on a
     bounded sample: chunks of `chunk` rows of the workload until `seconds` pass."""
@@ -365,7 +378,9 @@ def run_ours(args, rank, world, local_rank):
                            "parallelism": f"row-sharded x{world}, no collective in the step",
                            "l2": "two alternating input sets of 218 MB each (> 126 MB L2)"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                             "frac": achieved / peak, "traffic": None,
+                             "frac": achieved / peak, "traffic": profiled_traffic(),
+                             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                               "(profiles/stream_kernel_cfg4.md)",
                              "peak_source": peak_kind, "algorithmic_bytes_per_launch": per_launch,
                              "mean_launch_us": mean_kern_s * 1e6},
                 "cpu_baseline": cpu,
@@ -417,8 +432,10 @@ def latency_extras(sv, dev):
         rs = torch.from_numpy(d["running"]).to(dev)
         u = torch.from_numpy(d["uniforms"]).to(dev)
         ob = {}
-        sv.beam_step(x, rs, u, history=h, out=ob)
-        out[name] = graph_time_us(lambda: sv.beam_step(x, rs, u, history=h, out=ob))
+        # The workspace is allocated before capture (the graph then holds no fill).
+        ws = sv.beam_workspace(x.shape[0], x.shape[1], dev)
+        sv.beam_step(x, rs, u, history=h, out=ob, workspace=ws)
+        out[name] = graph_time_us(lambda: sv.beam_step(x, rs, u, history=h, out=ob, workspace=ws))
     t = torch.from_numpy(cfg5_tokens()).to(dev)
     lens = torch.full((t.shape[0],), t.shape[1], dtype=torch.int32, device=dev)
     v = torch.empty(t.shape[0], dtype=torch.uint8, device=dev)

@@ -169,17 +169,21 @@ def beam_step(logits, running_scores, uniforms, *, history=None, history_len=Non
         raise ValueError("uniforms must be a contiguous float32 tensor with num_picks values")
     hp, hk, hs, hl, hc, _keep = _history(B, V, history, history_len, seen, seen_bits)
     o = out if out is not None else {}  # filled in place: callers may preallocate
-    o.setdefault("picks", torch.full((P,), -1, dtype=torch.int64, device=dev))
-    o.setdefault("scores", torch.zeros(P, dtype=torch.float32, device=dev))
-    o.setdefault("n", torch.zeros(1, dtype=torch.int32, device=dev))
-    o.setdefault("status", torch.zeros(1, dtype=torch.int32, device=dev))
+    # Only missing outputs are allocated (a preallocated dict costs no kernels).
+    need = {"picks": lambda: torch.full((P,), -1, dtype=torch.int64, device=dev),
+            "scores": lambda: torch.zeros(P, dtype=torch.float32, device=dev),
+            "n": lambda: torch.zeros(1, dtype=torch.int32, device=dev),
+            "status": lambda: torch.zeros(1, dtype=torch.int32, device=dev)}
     if out_capacity:
-        o.setdefault("kept_count", torch.zeros(B, dtype=torch.int32, device=dev))
-        o.setdefault("kept_idx", torch.full((B, out_capacity), -1, dtype=torch.int32, device=dev))
-        o.setdefault("kept_logprob", torch.zeros((B, out_capacity), dtype=torch.float32, device=dev))
-        o.setdefault("kept_prob", torch.zeros((B, out_capacity), dtype=torch.float32, device=dev))
+        need.update(kept_count=lambda: torch.zeros(B, dtype=torch.int32, device=dev),
+                    kept_idx=lambda: torch.full((B, out_capacity), -1, dtype=torch.int32, device=dev),
+                    kept_logprob=lambda: torch.zeros((B, out_capacity), dtype=torch.float32, device=dev),
+                    kept_prob=lambda: torch.zeros((B, out_capacity), dtype=torch.float32, device=dev))
     if dense_logprob:
-        o.setdefault("dense_logprob", torch.empty((B, V), dtype=torch.float32, device=dev))
+        need["dense_logprob"] = lambda: torch.empty((B, V), dtype=torch.float32, device=dev)
+    for k, make in need.items():
+        if k not in o:
+            o[k] = make()
     ws = workspace if workspace is not None else beam_workspace(B, V, dev)
     rc = L.lib().sv_beam_step(
         x.data_ptr(), _DTYPES[x.dtype], B, V, x.stride(0) if B > 1 else 0, hp, hk, hs, hl, hc, rs.data_ptr(),
