@@ -12,9 +12,9 @@ The directory name is not a Python identifier (it is a ComfyUI custom-node folde
 load it by path, e.g. through __graft_entry__.load_package(), which registers it as
 `starvector_b200`.
 """
-from . import _lib
-from .ops import (beam_step, beam_workspace, loop_guard, penalize, sample_step, seen_bitmap, seen_reorder,
-                  seen_update)
+from . import _lib, sharded
+from .ops import (beam_step, beam_workspace, loop_guard, merge_shards, penalize, sample_step, seen_bitmap,
+                  seen_reorder, seen_update)
 
-__all__ = ["sample_step", "beam_step", "beam_workspace", "loop_guard", "penalize", "seen_bitmap", "seen_reorder",
-           "seen_update"]
+__all__ = ["sample_step", "beam_step", "beam_workspace", "loop_guard", "merge_shards", "penalize", "seen_bitmap",
+           "seen_reorder", "seen_update", "sharded"]

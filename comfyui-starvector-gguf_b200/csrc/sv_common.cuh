@@ -28,6 +28,7 @@ enum Status : int32_t {
   ST_ALLNEGINF = 3,   // no finite logit in the row
   ST_HISTORY = 4,     // a history id outside [0, V)
   ST_TIMEOUT = 5,     // a bounded wait on an asynchronous copy ran out
+  ST_SHARD_OVERFLOW = 6,  // vocab-sharded merge: a slice's kept list exceeded its capacity
 };
 
 __device__ __forceinline__ uint32_t ord_key(float f) {

@@ -244,3 +244,38 @@ def seen_reorder(src, dst, parents, tokens, vocab):
     rc = L.lib().sv_seen_reorder(src.data_ptr(), dst.data_ptr(), src.shape[0], int(vocab), src.stride(0),
                                  p.data_ptr(), _ptr(t), _stream(src.device))
     L.check(rc, "sv_seen_reorder")
+
+
+def merge_shards(packed, uniforms, *, capacity, top_p=0.9, top_k=50, keep=1, out_capacity=0, out=None):
+    """Merges the all-gathered per-slice kept lists of a vocab-sharded sample step
+    (sv_merge_shards): packed int32 [shards, rows, 2 * capacity + 2].
+
+    Returns a dict: token int64 [rows], count int32 [rows], status int32 [rows],
+    and idx / prob [rows, out_capacity] when out_capacity > 0.
+    """
+    _need_cuda(packed, "packed")
+    if packed.dtype != torch.int32 or packed.dim() != 3 or not packed.is_contiguous():
+        raise ValueError("packed must be a contiguous int32 tensor [shards, rows, 2 * capacity + 2]")
+    S, R, W = packed.shape
+    if W != 2 * capacity + 2:
+        raise ValueError("packed records must hold 2 * capacity + 2 values")
+    u = uniforms.reshape(-1)
+    _need_cuda(u, "uniforms")
+    if u.dtype != torch.float32 or not u.is_contiguous() or u.numel() < R:
+        raise ValueError("uniforms must be a contiguous float32 tensor with one value per row")
+    dev = packed.device
+    o = out if out is not None else {}
+    need = {"token": lambda: torch.empty(R, dtype=torch.int64, device=dev),
+            "count": lambda: torch.empty(R, dtype=torch.int32, device=dev),
+            "status": lambda: torch.empty(R, dtype=torch.int32, device=dev)}
+    if out_capacity:
+        need.update(idx=lambda: torch.full((R, out_capacity), -1, dtype=torch.int32, device=dev),
+                    prob=lambda: torch.zeros((R, out_capacity), dtype=torch.float32, device=dev))
+    for k, make in need.items():
+        if k not in o:
+            o[k] = make()
+    rc = L.lib().sv_merge_shards(packed.data_ptr(), S, R, int(capacity), u.data_ptr(), float(top_p), int(top_k),
+                                 int(keep), o["token"].data_ptr(), o["count"].data_ptr(), _ptr(o.get("idx")),
+                                 _ptr(o.get("prob")), int(out_capacity), o["status"].data_ptr(), _stream(dev))
+    L.check(rc, "sv_merge_shards")
+    return o

@@ -42,6 +42,7 @@ extern "C" {
 #define SV_ST_ALLNEGINF 3  /* no finite logit in the row */
 #define SV_ST_HISTORY 4    /* a history id outside [0, vocab) */
 #define SV_ST_TIMEOUT 5    /* a bounded wait on an asynchronous copy ran out */
+#define SV_ST_SHARD_OVERFLOW 6 /* sv_merge_shards: a slice's kept list exceeded its capacity */
 
 /* Logit dtypes. */
 #define SV_F32 0
@@ -183,6 +184,30 @@ int sv_seen_update(uint32_t* seen_bits, int32_t rows, int64_t row_stride_words, 
  * tokens may be NULL.  src and dst must not overlap. */
 int sv_seen_reorder(const uint32_t* src, uint32_t* dst, int32_t beams, int32_t vocab, int64_t row_stride_words,
                     const int64_t* parents, const int64_t* tokens, void* stream);
+
+/*
+ * Vocab-sharded sample step, merge side.  No single counterpart in the reference:
+ * it replaces runtime_shared.py:180-186 and :201 (top-k with ties, top-p, the draw)
+ * for a row whose vocabulary is split across ranks, each rank having run
+ * sv_sample_step on its slice with top_p = 1 and out_capacity = capacity (its kept
+ * list is then the slice's top-k with ties).  `packed` holds, for each of `shards`
+ * slices and each row, one int32 record of 2 * capacity + 2 values:
+ *   [0, capacity)             the kept tokens' warped scores (float bits, out_score)
+ *   [capacity, 2 * capacity)  their global indices (out_idx + the slice's offset)
+ *   2 * capacity              the slice's kept count (out_count)
+ *   2 * capacity + 1          the slice's status (out_status)
+ * laid out [shards][rows][record] (what an all-gather of each rank's [rows][record]
+ * produces).  Results equal sv_sample_step on the whole row with the same
+ * uniforms.  shards * capacity <= 1024; max(top_k, keep) <= capacity.  A row whose
+ * slice kept more than `capacity` tokens (a tie group) gets SV_ST_SHARD_OVERFLOW and
+ * must be sampled unsharded.
+ *   out_token int64 [rows]; out_count int32 [rows] (may be NULL); out_idx / out_prob
+ *   [rows, out_capacity] the kept tokens in index order and their probabilities
+ *   (may be NULL); out_status int32 [rows] (may be NULL)
+ */
+int sv_merge_shards(const int32_t* packed, int32_t shards, int32_t rows, int32_t capacity, const float* uniforms,
+                    double top_p, int32_t top_k, int32_t keep, int64_t* out_token, int32_t* out_count,
+                    int32_t* out_idx, float* out_prob, int32_t out_capacity, int32_t* out_status, void* stream);
 
 /* Text of a return or status code. */
 const char* sv_error_string(int32_t code);
