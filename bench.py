@@ -365,6 +365,8 @@ def run_ours(args, rank, world, local_rank):
     d2h = ROWS * 8
 
     extras = latency_extras(sv, dev) if rank == 0 and not args.no_extras else {}
+    if world > 1 and not args.no_extras:
+        extras.update(vocab_sharded_extra(sv, dev, rank, world))  # every rank takes part
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         rps, rows, dt = cpu_port_rows_per_s(sets[0]["host"], seconds=args.cpu_seconds)
@@ -443,6 +445,47 @@ def latency_extras(sv, dev):
     out["cfg5_loop_guard_us"] = graph_time_us(lambda: sv.loop_guard(t, lens, out=v))
     out["cfg5_loop_guard_GBps"] = t.numel() * 4 / (out["cfg5_loop_guard_us"] * 1e-6) / 1e9
     return out
+
+
+def vocab_sharded_extra(sv, dev, rank, world, steps=20, warmup=3):
+    """Config 5's vocab-sharded sample step: 256 rows, V split across the ranks
+    (slice step, one NCCL all-gather of the top-50 lists, merge on every rank).
+    Device time per step, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    rows, cap = 256, 64
+    w = V // world
+    off = rank * w
+    g = np.random.default_rng(5)  # the same rows on every rank
+    x = (2.0 * g.standard_normal((rows, V))).astype(np.float32)
+    ids = g.integers(0, V, (rows, 16384))
+    u = g.random(rows).astype(np.float32)
+    xd = torch.from_numpy(np.ascontiguousarray(x[:, off:off + w])).to(dev)
+    ud = torch.from_numpy(u).to(dev)
+    seen = np.zeros((rows, V), bool)
+    seen[np.arange(rows)[:, None], ids] = True
+    packed = np.packbits(seen, axis=1, bitorder="little")  # V is a multiple of 32
+    bits = torch.from_numpy(np.ascontiguousarray(packed).view(np.int32)).to(dev)
+    out = {}
+
+    def step():
+        sv.sharded.sample_step_vocab_sharded(xd, ud, offset=off, seen_bits=bits, capacity=cap, out=out)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    bad = int(out["status"].max().item())
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) * 1e3 / steps, float(bad)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"cfg5_vocab_sharded_us_per_step": float(t[0]), "cfg5_vocab_sharded_slices": world,
+            "cfg5_vocab_sharded_max_status": int(t[1])}
 
 
 def main():
