@@ -33,6 +33,7 @@ _SIGNATURES = {
     "sv_seen_update": (_I32, [_P, _I32, _I64, _P, _I32, _P]),
     "sv_seen_reorder": (_I32, [_P, _P, _I32, _I32, _I64, _P, _P, _P]),
     "sv_merge_shards": (_I32, [_P, _I32, _I32, _I32, _P, _D, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P]),
+    "sv_pack_slice": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _P, _P]),
     "sv_error_string": (C.c_char_p, [_I32]),
     "sv_abi_version": (_I32, []),
 }

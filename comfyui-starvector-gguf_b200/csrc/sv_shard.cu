@@ -109,11 +109,37 @@ __global__ void __launch_bounds__(MNT) merge_kernel(const MergeArgs m, const Row
   }
 }
 
+// One rank's exchange records from its slice step's outputs (one block per row).
+__global__ void pack_kernel(const int32_t* count, const int32_t* status, const int32_t* idx, const float* score,
+                            int cap, int offset, int32_t* out) {
+  const int row = blockIdx.x;
+  int32_t* r = out + (int64_t)row * (2 * cap + 2);
+  for (int j = threadIdx.x; j < cap; j += blockDim.x) {
+    r[j] = __float_as_int(score[(int64_t)row * cap + j]);
+    r[cap + j] = idx[(int64_t)row * cap + j] + offset;
+  }
+  if (threadIdx.x == 0) {
+    r[2 * cap] = count[row];
+    r[2 * cap + 1] = status[row];
+  }
+}
+
 }  // namespace
 
 }  // namespace sv
 
 using namespace sv;
+
+// One rank's records [rows][2 * capacity + 2] for sv_merge_shards; see
+// include/starvector_sampling.h.
+extern "C" int sv_pack_slice(const int32_t* count, const int32_t* status, const int32_t* idx, const float* score,
+                             int32_t rows, int32_t capacity, int32_t offset, int32_t* out_records, void* stream) {
+  if (!count || !status || !idx || !score || !out_records) return SV_E_ARG;
+  if (rows < 1 || capacity < 1 || capacity > kMergeMax || offset < 0) return SV_E_SHAPE;
+  pack_kernel<<<rows, 64, 0, static_cast<cudaStream_t>(stream)>>>(count, status, idx, score, capacity, offset,
+                                                                  out_records);
+  return cudaGetLastError() == cudaSuccess ? SV_OK : SV_E_CUDA;
+}
 
 // Merges the all-gathered per-shard kept lists of a vocab-sharded sample step; see
 // include/starvector_sampling.h.

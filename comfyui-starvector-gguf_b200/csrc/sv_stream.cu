@@ -334,19 +334,36 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
       }
       // Unit maxima, seen bits and this lane's group value.  A unit with a seen
       // token enters the group value through a lower bound of its penalised
-      // maximum: the penalty of its raw maximum, with the product rounded down (no
-      // division; the penalty is monotone and never raises a score).  Full chunks
+      // maximum.  Full chunks
       // of aligned rows (the common case) take a path without bounds checks, their
       // units at a fixed bit offset in consecutive bitmap words.
       float umax[UPT];
       uint32_t sb[UPT];
       float gsrc = NEG;
-      auto unit = [&](int j, float m, uint32_t bitsj) {
-        const float lo = __fmul_rd(m, m < 0.0f ? rp : rinv_lo);
+      auto unit = [&](int j, const float (&v)[EPU], float m, uint32_t bitsj) {
+        // At or below the unit's penalised maximum (the penalty is monotone and
+        // never raises a score; its lower bounds are products rounded down, no
+        // division): for a unit with a seen token, the penalty bound of its raw
+        // maximum, or, when that maximum reaches the bound (only such values can
+        // enter the histogram), the larger of its unseen elements' maximum and the
+        // penalty bound of its largest seen element.
+        float gv = m;
+        if (bitsj) {
+          gv = __fmul_rd(m, m < 0.0f ? rp : rinv_lo);
+          if (m >= te) {
+            float mu = NEG, ms = NEG;
+#pragma unroll
+            for (int e = 0; e < EPU; ++e) {
+              if ((bitsj >> e) & 1u) ms = fmaxf(ms, v[e]);
+              else mu = fmaxf(mu, v[e]);
+            }
+            gv = fmaxf(mu, __fmul_rd(ms, ms < 0.0f ? rp : rinv_lo));
+          }
+        }
         umax[j] = m;
         sb[j] = bitsj;
         rmx = max_nan(rmx, m);
-        gsrc = fmaxf(gsrc, bitsj ? lo : m);  // fmaxf drops NaN; rmx reports it
+        gsrc = fmaxf(gsrc, gv);  // fmaxf drops NaN; rmx reports it
       };
       if (aligned && un == SCU) {
         const int e0 = (u0 + tid) * EPU;
@@ -359,7 +376,7 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
           float m = v[0];
 #pragma unroll
           for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
-          unit(j, m, (bw[j * (SNT * EPU / 32)] >> shf) & ((1u << EPU) - 1u));
+          unit(j, v, m, (bw[j * (SNT * EPU / 32)] >> shf) & ((1u << EPU) - 1u));
         }
       } else {
 #pragma unroll
@@ -367,16 +384,18 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
           const int k = tid + j * SNT;
           float m = NEG;
           uint32_t b = 0;
+          float v[EPU];
+#pragma unroll
+          for (int e = 0; e < EPU; ++e) v[e] = NEG;
           if (k < un) {
             b = aligned ? (bits[((u0 + k) * EPU) >> 5] >> (((u0 + k) * EPU) & 31)) & ((1u << EPU) - 1u)
                         : unit_bits(bits, (int64_t)(u0 + k) * EPU - g.off_e, EPU, V);
-            float v[EPU];
             IO::load(slot, k, v);
             m = v[0];
 #pragma unroll
             for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
           }
-          unit(j, m, b);
+          unit(j, v, m, b);
         }
       }
       const float gm = fmaxf(gsrc, __shfl_xor_sync(0xffffffffu, gsrc, 1));  // lane-pair group value
@@ -477,7 +496,7 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
     const float uu = a.uniforms[row];
     const int nu = sh.unit_n;
     int status = sh.err ? first_err(sh.err) : ST_OK;
-    bool general = status == ST_OK && (a.force_slow || nu > UCAP);
+    bool general = status == ST_OK && a.force_slow;
     float* sval = reinterpret_cast<float*>(sh.work);
     int* sidx = reinterpret_cast<int*>(sh.work + 4 * SFIN);
     uint64_t* W = reinterpret_cast<uint64_t*>(sh.work + 8 * SFIN);
@@ -489,9 +508,28 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
     int m = 0;
     if (status == ST_OK && !general) {
       // The elements of the hit units whose penalised score reaches the final
-      // bound, tempered (elements outside the row were staged as -inf).
+      // bound, tempered (elements outside the row were staged as -inf).  When the
+      // list overflowed, the row is read again (from L2 or HBM) against that bound.
       int bad = 0;
-      for (int t = tid; t < nu; t += SNT) {
+      auto take = [&](int i, float x) {
+        const float tx = temper(x, T);
+        bad |= tx == PINF;
+        const int at = atomicAdd(&bs.flag, 1);
+        if (at < SFIN) {
+          fv[at] = tx;
+          fi[at] = i;
+        }
+      };
+      if (nu > UCAP) {
+        for (int64_t i = tid; i < V; i += SNT) {
+          float x = Elem<TIn>::load(rowp + i);
+          if (x >= tfin) {
+            if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
+            if (x >= tfin) take((int)i, x);
+          }
+        }
+      }
+      for (int t = tid; t < (nu > UCAP ? 0 : nu); t += SNT) {
         const int ent = sh.uidx[t];
         const int uid = ent >> 8;
         float v[EPU];
@@ -502,15 +540,7 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
             const int i = uid * EPU + e - g.off_e;
             float x = v[e];
             if ((ent >> e) & 1) x = penalize(x, rp);
-            if (x >= tfin) {
-              const float tx = temper(x, T);
-              bad |= tx == PINF;
-              const int at = atomicAdd(&bs.flag, 1);
-              if (at < SFIN) {
-                fv[at] = tx;
-                fi[at] = i;
-              }
-            }
+            if (x >= tfin) take(i, x);
           }
         }
       }

@@ -279,3 +279,18 @@ def merge_shards(packed, uniforms, *, capacity, top_p=0.9, top_k=50, keep=1, out
                                  _ptr(o.get("prob")), int(out_capacity), o["status"].data_ptr(), _stream(dev))
     L.check(rc, "sv_merge_shards")
     return o
+
+
+def pack_slice(local, offset, capacity, out):
+    """A rank's exchange records (sv_pack_slice) from its slice step's outputs
+    (count, status, idx, score [rows, capacity]) into out int32 [rows, 2C + 2]."""
+    for k in ("count", "status", "idx", "score"):
+        _need_cuda(local[k], k)
+    R = local["count"].shape[0]
+    if tuple(local["idx"].shape) != (R, capacity) or not out.is_contiguous():
+        raise ValueError("slice outputs must have capacity columns and the records be contiguous")
+    rc = L.lib().sv_pack_slice(local["count"].data_ptr(), local["status"].data_ptr(), local["idx"].data_ptr(),
+                               local["score"].data_ptr(), R, int(capacity), int(offset), out.data_ptr(),
+                               _stream(out.device))
+    L.check(rc, "sv_pack_slice")
+    return out

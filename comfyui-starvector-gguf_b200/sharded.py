@@ -61,6 +61,8 @@ def pack_slice(local, offset, capacity, out=None):
     R = local["token"].shape[0]
     rec = out if out is not None else torch.empty((R, record_width(capacity)), dtype=torch.int32,
                                                   device=local["token"].device)
+    if rec.is_cuda:
+        return ops.pack_slice(local, offset, capacity, rec)
     rec[:, :capacity] = local["score"].view(torch.int32)
     rec[:, capacity:2 * capacity] = local["idx"] + offset
     rec[:, 2 * capacity] = local["count"]

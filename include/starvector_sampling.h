@@ -209,6 +209,14 @@ int sv_merge_shards(const int32_t* packed, int32_t shards, int32_t rows, int32_t
                     double top_p, int32_t top_k, int32_t keep, int64_t* out_token, int32_t* out_count,
                     int32_t* out_idx, float* out_prob, int32_t out_capacity, int32_t* out_status, void* stream);
 
+/* Vocab-sharded sample step, one rank's side of the exchange: its records
+ * [rows][2 * capacity + 2] (the layout sv_merge_shards reads) from its slice step's
+ * out_count, out_status, out_idx and out_score ([rows, capacity]), with the slice's
+ * offset added to the ids.  No counterpart in the reference (it has no sharded
+ * vocabulary). */
+int sv_pack_slice(const int32_t* count, const int32_t* status, const int32_t* idx, const float* score, int32_t rows,
+                  int32_t capacity, int32_t offset, int32_t* out_records, void* stream);
+
 /* Text of a return or status code. */
 const char* sv_error_string(int32_t code);
 

@@ -204,6 +204,20 @@ def test_error_precedence_and_temperature_overflow(sv, path, force):
 
 
 @pytest.mark.parametrize("path", PATHS)
+def test_ascending_rows_and_dense_histories(sv, path):
+    """Rows whose scores rise along the vocabulary (every chunk beats the bound
+    so far: the streaming kernel's unit list overflows and the row is read again)
+    and histories covering a quarter of the vocabulary."""
+    g = np.random.default_rng(12)
+    V = 49152
+    x = (2 * g.standard_normal((8, V))).astype(np.float32)
+    x[:4] += np.linspace(0.0, 12.0, V, dtype=np.float32)
+    ids = g.integers(0, V, (8, 16384))
+    got, ref = run_both(sv, x, g.random(8).astype(np.float32), ids=ids, cap=128, path=path)
+    assert_same(got, ref)
+
+
+@pytest.mark.parametrize("path", PATHS)
 def test_history_out_of_range_is_reported(sv, path):
     x = torch.zeros((2, 1000), device=DEV)
     hist = torch.tensor([[1, 2, 3], [4, 1000, 5]], dtype=torch.int32, device=DEV)

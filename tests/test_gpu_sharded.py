@@ -48,12 +48,13 @@ def check(got, ref, cap):
         np.testing.assert_array_equal(got["prob"][r, :n], ref["prob"][r, :n])
 
 
-def test_cfg5_eight_slices_match_whole_row(sv):
+@pytest.mark.parametrize("hist", [2048, 16384])
+def test_cfg5_eight_slices_match_whole_row(sv, hist):
     """Config 5's split: V=49152 in 8 slices of 6144, top-50 lists, 256 rows."""
     g = np.random.default_rng(31)
     x = (2 * g.standard_normal((256, 49152))).astype(np.float32)
     seen = np.zeros(x.shape, np.uint8)
-    ids = g.integers(0, 49152, (256, 2048))
+    ids = g.integers(0, 49152, (256, hist))
     np.put_along_axis(seen, ids, 1, axis=1)
     u = g.random(256).astype(np.float32)
     got = run_sharded(sv, x, seen, u, shards=8, cap=64)
