@@ -82,7 +82,12 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
   uint64_t* Wg = reinterpret_cast<uint64_t*>(a.ws + sizeof(BeamWsHeader) + (size_t)B * a.ws_cap * 8);
   __shared__ int offs[kMaxBeams + 1];
   __shared__ int picked[2 * kMaxBeams];
+  __shared__ float uni[64];             // the draws' uniforms (num_picks <= 64)
+  __shared__ float run[kMaxBeams];      // running scores
   BlockScratch<NT>& bs = sh.bs;
+  // Loaded ahead: the draws are sequential and must not wait on memory each.
+  if (tid < a.npick) uni[tid] = a.uniforms[tid];
+  if (tid < B) run[tid] = a.running[tid];
   if (tid == 0) {
     int st = ST_OK, o = 0;
     for (int b = 0; b < B; ++b) {
@@ -109,14 +114,27 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
     while (offs[b + 1] <= e) ++b;
     return b;
   };
+  // Scores (+ running score) and flattened ids staged in shared memory in one pass
+  // when they fit.
+  const bool in_smem = K <= 1024;
+  float* es = reinterpret_cast<float*>(regA);
+  uint64_t* W = in_smem ? reinterpret_cast<uint64_t*>(regA + 4096) : Wg;
+  int64_t* ef = reinterpret_cast<int64_t*>(regA + 12288);  // K <= 512 only
+  const bool ids_smem = K <= 512;
   auto score_of = [&](int e, int b) -> float {
-    return __fadd_rn(__ldcg(&kval0[(size_t)b * a.ws_cap + (e - offs[b])]), a.running[b]);
+    return in_smem ? es[e] : __fadd_rn(__ldcg(&kval0[(size_t)b * a.ws_cap + (e - offs[b])]), run[b]);
   };
+  if (in_smem) {
+    for (int e = tid; e < K; e += NT) {
+      const int b = beam_of(e);
+      es[e] = __fadd_rn(__ldcg(&kval0[(size_t)b * a.ws_cap + (e - offs[b])]), run[b]);
+      if (ids_smem) ef[e] = (int64_t)b * a.vocab + __ldcg(&kidx0[(size_t)b * a.ws_cap + (e - offs[b])]);
+    }
+    __syncthreads();
+  }
   float mx = Elem<float>::neg_inf();
   for (int e = tid; e < K; e += NT) mx = max_nan(mx, score_of(e, beam_of(e)));
   const float Ms = block_max_nan<NT>(bs, mx);
-  const bool in_smem = K <= 2048;
-  uint64_t* W = in_smem ? reinterpret_cast<uint64_t*>(regA) : Wg;
   uint64_t ls = 0;
   for (int e = tid; e < K; e += NT) {
     const float s = score_of(e, beam_of(e));
@@ -141,21 +159,24 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
     const int e0 = lane * seg, e1 = min(K, e0 + seg);
     uint64_t mysum = 0;
     for (int e = e0; e < e1; ++e) mysum += W[e];
+    // Inclusive prefix of the lanes' segment sums and the total, scanned once and
+    // then updated as picks remove weight.
+    uint64_t incl = mysum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    uint64_t total = __shfl_sync(0xffffffffu, incl, 31);
     for (int j = 0; j < n; ++j) {
-      const uint64_t total = warp_sum_u64(mysum);
       int pick = -1;
       if (total > 0) {
-        const uint64_t t = mulfloor(total, a.uniforms[j]);
-        uint64_t incl = mysum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          uint64_t v = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += v;
-        }
+        const uint64_t t = mulfloor(total, uni[j]);
         const uint64_t excl = incl - mysum;
         const bool own = mysum > 0 && excl <= t && t < incl;
         const unsigned bm = __ballot_sync(0xffffffffu, own);
         const int o = __ffs(bm) - 1;
+        uint64_t w = 0;
         if (lane == o) {
           uint64_t c = excl;
           for (int e = e0; e < e1; ++e) {
@@ -165,10 +186,14 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
               break;
             }
           }
-          mysum -= W[pick];
+          w = W[pick];
+          mysum -= w;
           W[pick] = 0;
         }
         pick = __shfl_sync(0xffffffffu, pick, o);
+        w = __shfl_sync(0xffffffffu, w, o);
+        if (lane >= o) incl -= w;
+        total -= w;
       } else {
         // No fixed-point mass left: the largest remaining nonzero probability.
         float best = -1.0f;
@@ -194,13 +219,16 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
         }
         pick = be;
       }
-      if (lane == 0) {
-        picked[j] = pick;
-        const int b = beam_of(pick);
-        a.out_picks[j] = (int64_t)b * a.vocab + __ldcg(&kidx0[(size_t)b * a.ws_cap + (pick - offs[b])]);
-        a.out_pick_scores[j] = score_of(pick, b);
-      }
+      if (lane == 0) picked[j] = pick;
       __syncwarp();
+    }
+    // The picks' outputs, one lane each, off the draws' dependency chain.
+    for (int j = lane; j < n; j += 32) {
+      const int pick = picked[j];
+      const int b = beam_of(pick);
+      a.out_picks[j] = in_smem && ids_smem ? ef[pick]
+                                           : (int64_t)b * a.vocab + __ldcg(&kidx0[(size_t)b * a.ws_cap + (pick - offs[b])]);
+      a.out_pick_scores[j] = score_of(pick, b);
     }
     if (lane == 0) {
       *a.out_npicks = n;
@@ -483,10 +511,35 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
     if (!a.force_slow && n <= CAP) {
       float* fv = reinterpret_cast<float*>(W);
       int* fi = reinterpret_cast<int*>(regA + 12 * CAP);
-      const int m = prefilter<NT>(bs, sh.cand_val, sh.cand_idx, n, a.kk, fv, fi);
-      kept = leader_fast<NT>(a, bs, fv, fi, m, sval, sidx, W, reinterpret_cast<uint64_t*>(sh.cand_val), kidx, kval);
+      // Up to 128 candidates: one warp finishes in registers (after the exact
+      // prefilter when there are more).
+      const float* cv = sh.cand_val;
+      const int* ci = sh.cand_idx;
+      int m = n;
+      if (n > 128) {
+        m = prefilter<NT>(bs, sh.cand_val, sh.cand_idx, n, a.kk, fv, fi);
+        cv = fv;
+        ci = fi;
+      }
+      if (m <= 128) {
+        if (tid < 32) {
+          kept = m <= 64 ? warp_finish<2>(a, cv, ci, m, uu, &token, kidx, kval)
+                         : warp_finish<4>(a, cv, ci, m, uu, &token, kidx, kval);
+          if (tid == 0) {
+            bs.flag2 = kept.n;
+            bs.fval = kept.M;
+            bs.u64a = kept.tot;
+          }
+        }
+        __syncthreads();
+        kept.n = bs.flag2;
+        kept.M = bs.fval;
+        kept.tot = bs.u64a;
+      } else {
+        kept = leader_fast<NT>(a, bs, fv, fi, m, sval, sidx, W, reinterpret_cast<uint64_t*>(sh.cand_val), kidx, kval);
+        if (MODE == MODE_SAMPLE) token = draw_kept<NT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(regA));
+      }
       const float Sf = fix_to_float(kept.tot);
-      if (MODE == MODE_SAMPLE) token = draw_kept<NT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(regA));
       for (int j = tid; j < kept.n; j += NT) {
         const float p = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kept.M)), Sf);
         if (j < a.out_cap) {
