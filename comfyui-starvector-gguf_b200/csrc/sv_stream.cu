@@ -54,6 +54,8 @@ constexpr int SBINS = 256;              // bound histogram bins
 constexpr int UCAP = 704;               // hit units per row (their 16 bytes are kept)
 constexpr int SFIN = 256;               // candidates the fast finish handles after pruning
 constexpr int kBoundWarp = SWARPS - 1;  // computes the histogram bound after each chunk
+constexpr int kIssuer = 32;             // issues the bulk copies (warp 1: warp 0 may be finishing a row)
+constexpr int NB = SNT - 32;            // threads of warps 1.. that build a row's seen bitmap
 
 struct __align__(16) StreamShared {
   unsigned long long mbar[SBUF];
@@ -75,6 +77,10 @@ constexpr size_t kStaticBytes = (sizeof(StreamShared) + 127) & ~size_t(127);
 __host__ __device__ inline size_t bitmap_bytes(int64_t V) {
   return (((size_t)V + 31) / 32 * 4 + 16 + 127) & ~size_t(127);
 }
+
+// Warps 1.. only (the row-start bitmap build, while warp 0 may still finish the
+// previous row).
+__device__ __forceinline__ void bar_builders() { asm volatile("bar.sync 1, %0;" ::"n"(NB) : "memory"); }
 
 // Geometry of one row's window: 16-byte units from the row start rounded down.
 struct RowGeom {
@@ -161,13 +167,13 @@ __device__ __forceinline__ float hist_bound(const unsigned int* bins, uint32_t b
   return lower_tau(key_to_float(base_key + ((uint32_t)best << shift)), T);
 }
 
-// Marks history ids staged in shared memory (16-byte vectors of Id) in the bitmap;
-// returns the ST_HISTORY error bit for ids outside [0, V).
+// Marks history ids staged in shared memory (16-byte vectors of Id) in the bitmap
+// (threads 32..); returns the ST_HISTORY error bit for ids outside [0, V).
 template <typename Id>
 __device__ __forceinline__ int mark_staged(const unsigned char* src, int64_t L, int64_t V, uint32_t* bits) {
   constexpr int PER = 16 / (int)sizeof(Id);
   int err = 0;
-  for (int64_t q = threadIdx.x; q * PER < L; q += SNT) {
+  for (int64_t q = threadIdx.x - 32; q * PER < L; q += NB) {
     Id id[PER];
     *reinterpret_cast<uint4*>(id) = reinterpret_cast<const uint4*>(src)[q];
 #pragma unroll
@@ -225,7 +231,7 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
     sh.err = 0;
   }
   __syncthreads();
-  auto issue_next = [&]() {  // thread 0, after a block barrier
+  auto issue_next = [&]() {  // thread kIssuer, after a barrier
     if (irow >= a.rows) return;
     fence_proxy_async_smem();
     const int s = islot;
@@ -244,7 +250,7 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
       if (irow < a.rows) ig = row_geom<TIn>(a, irow);
     }
   };
-  if (tid == 0)
+  if (tid == kIssuer)
     for (int s = 0; s < SBUF; ++s) issue_next();
 
   // Ring slot and mbarrier phase of the next slot to consume (all threads).
@@ -261,51 +267,56 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
     const RowGeom g = row_geom<TIn>(a, row);
     const TIn* rowp = reinterpret_cast<const TIn*>(a.logits) + row * a.row_stride;
     const bool aligned = g.off_e == 0;
-    // 1. seen bitmap of the row.
-    {
-      const int nz = (nw + 4 + 3) >> 2;  // 16-byte words, within bitmap_bytes(V)
-      for (int w = tid; w < nz; w += SNT) reinterpret_cast<uint4*>(bits)[w] = make_uint4(0, 0, 0, 0);
-    }
-    if (tid < SBINS / 4) reinterpret_cast<uint4*>(sh.bins)[tid] = make_uint4(0, 0, 0, 0);
-    if (tid == 0) {
-      sh.unit_n = 0;
-      sh.te_pub = NEG;
-      sh.rmax_key = 0;
-    }
-    __syncthreads();
-    int local_err = 0;
-    if (ids_kind) {
-      const int64_t L = hist_length(a, row);
-      if (stage_ids) {
-        if (!mbar_wait(&sh.mbar[cslot], cphase)) local_err |= 1 << ST_TIMEOUT;
-        const unsigned char* src = ring + (size_t)cslot * SCHUNK;
-        local_err |= idb == 4 ? mark_staged<int32_t>(src, L, V, bits) : mark_staged<int64_t>(src, L, V, bits);
-        consume_next();
-        __syncthreads();  // the ids slot is consumed
-        if (tid == 0) issue_next();
-      } else {
-        for (int64_t j = tid; j < L; j += SNT) {
-          const int64_t x = hist_id(a, row, j);
-          if (x < 0 || x >= V) {
-            local_err |= 1 << ST_HISTORY;
-          } else {
-            const uint32_t b = 1u << (x & 31);
-            if (!(bits[x >> 5] & b)) atomicOr(&bits[x >> 5], b);
+    // 1. seen bitmap of the row, by warps 1.. (warp 0 may still be finishing the
+    //    previous row; it joins at the barrier before the chunks).
+    if (warp > 0) {
+      const int bt = tid - 32;
+      {
+        const int nz = (nw + 4 + 3) >> 2;  // 16-byte words, within bitmap_bytes(V)
+        for (int w = bt; w < nz; w += NB) reinterpret_cast<uint4*>(bits)[w] = make_uint4(0, 0, 0, 0);
+      }
+      if (bt < SBINS / 4) reinterpret_cast<uint4*>(sh.bins)[bt] = make_uint4(0, 0, 0, 0);
+      if (tid == kIssuer) {
+        sh.unit_n = 0;
+        sh.te_pub = NEG;
+        sh.rmax_key = 0;
+        sh.err = 0;
+      }
+      bar_builders();
+      int local_err = 0;
+      if (ids_kind) {
+        const int64_t L = hist_length(a, row);
+        if (stage_ids) {
+          if (!mbar_wait(&sh.mbar[cslot], cphase)) local_err |= 1 << ST_TIMEOUT;
+          const unsigned char* src = ring + (size_t)cslot * SCHUNK;
+          local_err |= idb == 4 ? mark_staged<int32_t>(src, L, V, bits) : mark_staged<int64_t>(src, L, V, bits);
+          bar_builders();  // the ids slot is consumed
+          if (tid == kIssuer) issue_next();
+        } else {
+          for (int64_t j = bt; j < L; j += NB) {
+            const int64_t x = hist_id(a, row, j);
+            if (x < 0 || x >= V) {
+              local_err |= 1 << ST_HISTORY;
+            } else {
+              const uint32_t b = 1u << (x & 31);
+              if (!(bits[x >> 5] & b)) atomicOr(&bits[x >> 5], b);
+            }
           }
         }
+      } else if (a.hist_kind == HIST_BITS32) {
+        const uint32_t* hb = reinterpret_cast<const uint32_t*>(a.hist) + row * a.hist_stride;
+        for (int w = bt; w < nw; w += NB) {
+          uint32_t v = hb[w];
+          if (w == nw - 1 && (V & 31)) v &= (1u << (V & 31)) - 1u;
+          bits[w] = v;
+        }
+      } else if (a.hist_kind == HIST_MASK8) {
+        for (int64_t i = bt; i < V; i += NB)
+          if (seen_global(a, row, i)) atomicOr(&bits[i >> 5], 1u << (i & 31));
       }
-    } else if (a.hist_kind == HIST_BITS32) {
-      const uint32_t* hb = reinterpret_cast<const uint32_t*>(a.hist) + row * a.hist_stride;
-      for (int w = tid; w < nw; w += SNT) {
-        uint32_t v = hb[w];
-        if (w == nw - 1 && (V & 31)) v &= (1u << (V & 31)) - 1u;
-        bits[w] = v;
-      }
-    } else if (a.hist_kind == HIST_MASK8) {
-      for (int64_t i = tid; i < V; i += SNT)
-        if (seen_global(a, row, i)) atomicOr(&bits[i >> 5], 1u << (i & 31));
+      if (local_err) atomicOr(&sh.err, local_err);
     }
-    if (local_err) atomicOr(&sh.err, local_err);
+    if (stage_ids) consume_next();  // every thread keeps the ring position
     __syncthreads();
 
     // 2. chunks.
@@ -477,7 +488,7 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
       }
       __syncthreads();  // the slot is consumed
       te = fmaxf(te, sh.te_pub);
-      if (tid == 0) issue_next();
+      if (tid == kIssuer) issue_next();
     }
     // The final bound, from the complete bins.
     if (warp == kBoundWarp) {
@@ -582,7 +593,6 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
           if (a.out_count) a.out_count[row] = kp.n;
           if (a.out_status) a.out_status[row] = ST_OK;
           if (a.seen_bits && tok >= 0) atomicOr(&a.seen_bits[row * a.seen_bits_stride + (tok >> 5)], 1u << (tok & 31));
-          sh.err = 0;
         }
       }
       continue;
@@ -644,7 +654,6 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
       if (a.out_status) a.out_status[row] = status;
       if (status == ST_OK && a.seen_bits && token >= 0)
         atomicOr(&a.seen_bits[row * a.seen_bits_stride + (token >> 5)], 1u << (token & 31));
-      sh.err = 0;
     }
     __syncthreads();
   }
