@@ -237,6 +237,176 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
   }
 }
 
+// Small kept lists (two beams of top-k 50 fit: 64 slots a beam): warp 0 alone
+// merges in registers, with no block barrier.  Lane L holds beam b = L / (32 / B) and slots
+// (L % (32 / B)) * kMergeR .. + kMergeR - 1 of that beam's kept list, so lane order
+// then slot order is the flattened (beam-major, index-ascending) order of
+// runtime_shared.py:231 and slots past a beam's count carry no weight.  The counts,
+// statuses and slots are loaded together, in one round trip to L2.  Returns false,
+// having written nothing, when a beam keeps more entries than its lanes hold; the
+// block merge then runs.  Same arithmetic as beam_merge, element for element.
+constexpr int kMergeR = 4;
+
+__device__ bool beam_merge_warp(const RowArgs& a) {
+  const int lane = threadIdx.x & 31;
+  const int B = a.rows;
+  const int LB = 32 / B;  // lanes per beam (B <= kMaxBeams = 32)
+  const int b = lane / LB;
+  const bool act = b < B;
+  const int j0 = (lane - b * LB) * kMergeR;
+  const BeamWsHeader* hdr = reinterpret_cast<const BeamWsHeader*>(a.ws);
+  const int* kidx0 = reinterpret_cast<const int*>(a.ws + sizeof(BeamWsHeader));
+  const float* kval0 = reinterpret_cast<const float*>(a.ws + sizeof(BeamWsHeader) + (size_t)B * a.ws_cap * 4);
+  const float NEG = Elem<float>::neg_inf();
+  int cnt = 0, stt = ST_OK;
+  float runb = 0.0f;
+  float s[kMergeR];  // kept log-probability + running score
+  int ki[kMergeR];
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) {
+    s[r] = 0.0f;
+    ki[r] = 0;
+  }
+  if (act) {
+    cnt = __ldcg(&hdr->count[b]);
+    stt = __ldcg(&hdr->status[b]);
+    runb = a.running[b];
+#pragma unroll
+    for (int r = 0; r < kMergeR; ++r) {
+      const int j = j0 + r;
+      if (j < a.ws_cap) {
+        s[r] = __ldcg(&kval0[(size_t)b * a.ws_cap + j]);
+        ki[r] = __ldcg(&kidx0[(size_t)b * a.ws_cap + j]);
+      }
+    }
+  }
+  const float u0 = lane < a.npick ? a.uniforms[lane] : 0.0f;
+  const float u1 = lane + 32 < a.npick ? a.uniforms[lane + 32] : 0.0f;
+  if (__ballot_sync(0xffffffffu, act && cnt > LB * kMergeR)) return false;
+  const unsigned bad = __ballot_sync(0xffffffffu, act && stt != ST_OK);
+  const int st = bad ? __shfl_sync(0xffffffffu, stt, __ffs(bad) - 1) : ST_OK;
+  const int K = warp_sum_int(act && lane == b * LB ? cnt : 0);
+  if (st != ST_OK || K == 0) {
+    if (lane == 0) {
+      *a.out_npicks = 0;
+      a.out_status[0] = st != ST_OK ? st : ST_ALLNEGINF;
+    }
+    return true;
+  }
+  unsigned valid = 0;
+  float mx = NEG;
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) {
+    const bool v = act && j0 + r < cnt;
+    valid |= (unsigned)v << r;
+    s[r] = __fadd_rn(s[r], runb);
+    if (v) mx = max_nan(mx, s[r]);
+  }
+  const float Ms = warp_max_nan(mx);
+  uint64_t W[kMergeR];
+  float ex[kMergeR];
+  uint64_t lsum = 0;
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) {
+    const bool v = (valid >> r) & 1u;
+    ex[r] = v ? sv_exp(__fsub_rn(s[r], Ms)) : 0.0f;
+    W[r] = fixw(ex[r]);
+    lsum += W[r];
+  }
+  const uint64_t tot = warp_sum_u64(lsum);
+  const float Sf = fix_to_float(tot);
+  int nz = 0;
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) {
+    if (!((valid >> r) & 1u)) continue;
+    const float p = __fdiv_rn(ex[r], Sf);
+    nz += p > 0.0f;
+    const int j = j0 + r;
+    if (a.out_prob && j < a.out_cap) a.out_prob[(size_t)b * a.out_cap + j] = p;
+  }
+  const int nnz = warp_sum_int(nz);
+  const int n = a.npick < nnz ? a.npick : nnz;
+  uint64_t lexcl = warp_incl_scan_u64(lsum) - lsum;
+  uint64_t total = tot;
+  unsigned taken = 0;
+  for (int j = 0; j < n; ++j) {
+    const float uj = __shfl_sync(0xffffffffu, j < 32 ? u0 : u1, j & 31);
+    int owner, rs = -1;
+    if (total > 0) {
+      // The element whose fixed-point interval holds floor(total * u): its lane
+      // first, then its slot by a walk of the lane's weights.
+      const uint64_t t = mulfloor(total, uj);
+      const bool own = lsum > 0 && lexcl <= t && t < lexcl + lsum;
+      owner = __ffs(__ballot_sync(0xffffffffu, own)) - 1;
+      uint64_t w = 0;
+      if (lane == owner) {
+        uint64_t c = lexcl;
+#pragma unroll
+        for (int r = 0; r < kMergeR; ++r) {
+          c += W[r];
+          if (rs < 0 && c > t) rs = r;
+        }
+#pragma unroll
+        for (int r = 0; r < kMergeR; ++r)
+          if (r == rs) {
+            w = W[r];
+            W[r] = 0;
+          }
+        lsum -= w;
+      }
+      w = __shfl_sync(0xffffffffu, w, owner);
+      if (lane > owner) lexcl -= w;
+      total -= w;
+    } else {
+      // No fixed-point mass left: the largest remaining nonzero probability,
+      // ties to the lowest flattened position.
+      float best = -1.0f;
+      int be = 0x7fffffff;
+#pragma unroll
+      for (int r = 0; r < kMergeR; ++r) {
+        if (!((valid >> r) & 1u) || ((taken >> r) & 1u)) continue;
+        const float p = __fdiv_rn(sv_exp(__fsub_rn(s[r], Ms)), Sf);
+        if (p > 0.0f && p > best) {
+          best = p;
+          be = lane * kMergeR + r;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+        if (ob > best || (ob == best && oe < be)) {
+          best = ob;
+          be = oe;
+        }
+      }
+      owner = be / kMergeR;
+      rs = be - owner * kMergeR;
+    }
+    if (lane == owner) {
+      // The pick's outputs from the owner's registers.
+#pragma unroll
+      for (int r = 0; r < kMergeR; ++r)
+        if (r == rs) {
+          taken |= 1u << r;
+          a.out_picks[j] = (int64_t)b * a.vocab + ki[r];
+          a.out_pick_scores[j] = s[r];
+        }
+    }
+  }
+  if (lane == 0) {
+    *a.out_npicks = n;
+    a.out_status[0] = ST_OK;
+  }
+  return true;
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // ------------------------------------------------------------------ the kernel
 
 template <typename TIn, int MODE>
@@ -601,13 +771,19 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
     hdr->count[row] = kept.n;
     if (a.out_count) a.out_count[row] = kept.n;
   }
-  __threadfence();
+  // The barrier orders the block's kept-list writes before thread 0's atomic,
+  // whose release publishes them and whose acquire (in the last leader) orders
+  // the other leaders' lists before the merge's reads.
   __syncthreads();
-  if (tid == 0) bs.flag = atomicAdd(&hdr->counter, 1u) == (unsigned)(a.rows - 1);
+  if (tid == 0) bs.flag = atom_add_acq_rel_gpu(&hdr->counter, 1u) == (unsigned)(a.rows - 1);
   __syncthreads();
   if (!bs.flag) return;
-  __threadfence();
-  beam_merge(a, sh, regA);
+  if (tid < 32) {
+    const bool done = !a.force_slow && beam_merge_warp(a);
+    if (tid == 0) bs.flag2 = done;
+  }
+  __syncthreads();
+  if (!bs.flag2) beam_merge(a, sh, regA);
   __syncthreads();
   if (tid == 0) atomicExch(&hdr->counter, 0u);
 }

@@ -148,3 +148,35 @@ def test_workspace_reuse_across_calls(sv):
     for _ in range(5):
         o = sv.beam_step(x, rs, u, history=h)
         assert torch.equal(o["picks"], picks)
+
+
+@pytest.mark.parametrize("force", [False, True], ids=["warp", "block"])
+@pytest.mark.parametrize("beams,top_k", [(1, 50), (2, 50), (2, 64), (3, 30), (8, 12), (16, 6), (32, 3)])
+def test_register_merge_shapes(sv, beams, top_k, force):
+    """Kept lists that fit the one-warp register merge (lanes split across beams)
+    and the same inputs through the block merge; several seeds each."""
+    for seed in range(3):
+        g = np.random.default_rng(100 + 7 * beams + seed)
+        x = (2 * g.standard_normal((beams, 2048))).astype(np.float32)
+        running = np.sort(g.uniform(-30, 0, beams)).astype(np.float32)[::-1].copy()
+        u = g.random(2 * beams).astype(np.float32)
+        got, ref = run_both(sv, x, running, u, ids=g.integers(0, 2048, (beams, 300)), top_k=top_k, p=0.97,
+                            force=force)
+        assert_same(got, ref)
+
+
+@pytest.mark.parametrize("force", [False, True], ids=["warp", "block"])
+@pytest.mark.parametrize("lag", [20.0, 45.0, 70.0])
+def test_merge_mass_below_fixed_point(sv, lag, force):
+    """One dominant continuation and a second beam far behind: after the first
+    pick the remaining candidates have probabilities above zero but no
+    fixed-point weight, so the later picks take the largest remaining
+    probability (runtime_shared.py:233-235)."""
+    g = np.random.default_rng(int(lag))
+    x = (2 * g.standard_normal((2, 4096))).astype(np.float32)
+    x[0, 17] += 40.0
+    running = np.array([0.0, -lag], np.float32)
+    u = g.random(4).astype(np.float32)
+    got, ref = run_both(sv, x, running, u, force=force)
+    assert ref["n"] >= 2
+    assert_same(got, ref)
