@@ -56,6 +56,12 @@ struct __align__(16) Shared {
   int cand_idx[CAP];
 };
 
+// Named barrier 1: warp 0 arrives (producer), the other warps wait (consumers).
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
 __device__ __forceinline__ void cluster_arrive_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
@@ -71,6 +77,12 @@ __device__ __forceinline__ T* remote(cg::cluster_group& cl, T* p, int rank) {
 }
 
 // ------------------------------------------------------------------ beam merge
+// A NaN flattened score (runtime_shared.py:231): a NaN running score, or +inf
+// added to the -inf of a beam's entries outside its kept list.
+__device__ __forceinline__ bool running_gives_nan(float rs, int count, int64_t vocab) {
+  return rs != rs || (rs == __int_as_float(0x7f800000) && (int64_t)count < vocab);
+}
+
 // Runs in the last beam leader to finish.  Entries of all beams in flattened
 // (beam-major, index-ascending) order.
 __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
@@ -90,14 +102,17 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
   if (tid < B) run[tid] = a.running[tid];
   if (tid == 0) {
     int st = ST_OK, o = 0;
+    bool nan_score = false;
     for (int b = 0; b < B; ++b) {
       const int s = __ldcg(&hdr->status[b]);
+      const int c = __ldcg(&hdr->count[b]);
       if (s != ST_OK && st == ST_OK) st = s;
+      nan_score |= running_gives_nan(a.running[b], c, a.vocab);
       offs[b] = o;
-      o += __ldcg(&hdr->count[b]);
+      o += c;
     }
     offs[B] = o;
-    bs.flag = st;
+    bs.flag = st == ST_OK && nan_score ? ST_NAN : st;
   }
   __syncthreads();
   const int st = bs.flag;
@@ -135,6 +150,13 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
   float mx = Elem<float>::neg_inf();
   for (int e = tid; e < K; e += NT) mx = max_nan(mx, score_of(e, beam_of(e)));
   const float Ms = block_max_nan<NT>(bs, mx);
+  if (Ms == __int_as_float(0x7f800000) || Ms == Elem<float>::neg_inf()) {
+    if (tid == 0) {
+      *a.out_npicks = 0;
+      a.out_status[0] = Ms > 0.0f ? ST_POSINF : ST_ALLNEGINF;
+    }
+    return;
+  }
   uint64_t ls = 0;
   for (int e = tid; e < K; e += NT) {
     const float s = score_of(e, beam_of(e));
@@ -247,6 +269,19 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
 // block merge then runs.  Same arithmetic as beam_merge, element for element.
 constexpr int kMergeR = 4;
 
+// Loads issued where they are written: the merge's inputs are all requested in one
+// round trip before the first use, and the compiler neither sinks nor splits them.
+__device__ __forceinline__ float ld_now(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_now(const int* p) {
+  int v;
+  asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ bool beam_merge_warp(const RowArgs& a) {
   const int lane = threadIdx.x & 31;
   const int B = a.rows;
@@ -267,24 +302,26 @@ __device__ bool beam_merge_warp(const RowArgs& a) {
     s[r] = 0.0f;
     ki[r] = 0;
   }
+  float u0 = 0.0f, u1 = 0.0f;
+  if (lane < a.npick) u0 = ld_now(&a.uniforms[lane]);
+  if (lane + 32 < a.npick) u1 = ld_now(&a.uniforms[lane + 32]);
   if (act) {
-    cnt = __ldcg(&hdr->count[b]);
-    stt = __ldcg(&hdr->status[b]);
-    runb = a.running[b];
+    cnt = ld_now(&hdr->count[b]);
+    stt = ld_now(&hdr->status[b]);
+    runb = ld_now(&a.running[b]);
 #pragma unroll
     for (int r = 0; r < kMergeR; ++r) {
       const int j = j0 + r;
       if (j < a.ws_cap) {
-        s[r] = __ldcg(&kval0[(size_t)b * a.ws_cap + j]);
-        ki[r] = __ldcg(&kidx0[(size_t)b * a.ws_cap + j]);
+        s[r] = ld_now(&kval0[(size_t)b * a.ws_cap + j]);
+        ki[r] = ld_now(&kidx0[(size_t)b * a.ws_cap + j]);
       }
     }
   }
-  const float u0 = lane < a.npick ? a.uniforms[lane] : 0.0f;
-  const float u1 = lane + 32 < a.npick ? a.uniforms[lane + 32] : 0.0f;
   if (__ballot_sync(0xffffffffu, act && cnt > LB * kMergeR)) return false;
   const unsigned bad = __ballot_sync(0xffffffffu, act && stt != ST_OK);
-  const int st = bad ? __shfl_sync(0xffffffffu, stt, __ffs(bad) - 1) : ST_OK;
+  const bool nan_score = __any_sync(0xffffffffu, act && running_gives_nan(runb, cnt, a.vocab));
+  const int st = bad ? __shfl_sync(0xffffffffu, stt, __ffs(bad) - 1) : (nan_score ? ST_NAN : ST_OK);
   const int K = warp_sum_int(act && lane == b * LB ? cnt : 0);
   if (st != ST_OK || K == 0) {
     if (lane == 0) {
@@ -303,6 +340,13 @@ __device__ bool beam_merge_warp(const RowArgs& a) {
     if (v) mx = max_nan(mx, s[r]);
   }
   const float Ms = warp_max_nan(mx);
+  if (Ms == __int_as_float(0x7f800000) || Ms == NEG) {
+    if (lane == 0) {
+      *a.out_npicks = 0;
+      a.out_status[0] = Ms > 0.0f ? ST_POSINF : ST_ALLNEGINF;
+    }
+    return true;
+  }
   uint64_t W[kMergeR];
   float ex[kMergeR];
   uint64_t lsum = 0;
@@ -671,6 +715,7 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
   int status = err ? first_err(err) : ST_OK;
   Kept kept = {0, 0.0f, 0};
   int64_t token = -1;
+  bool published = false;  // beam: kept list already published by warp 0
   const int n = sh.cand_n;
   // The row maximum is always a candidate when it is finite (tau <= max).
   if (status == ST_OK && n == 0) status = ST_ALLNEGINF;
@@ -691,7 +736,43 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
         cv = fv;
         ci = fi;
       }
-      if (m <= 128) {
+      if (m <= 128 && MODE == MODE_BEAM) {
+        // Warp 0 finishes, publishes the kept list and, in the last leader, merges
+        // the beams; the other warps write this beam's kept outputs meanwhile.
+        published = true;
+        if (tid < 32) {
+          kept = m <= 64 ? warp_finish<2>(a, cv, ci, m, uu, &token, kidx, kval)
+                         : warp_finish<4>(a, cv, ci, m, uu, &token, kidx, kval);
+          if (tid == 0) {
+            bs.flag2 = kept.n;
+            bs.fval = kept.M;
+            bs.u64a = kept.tot;
+          }
+          named_arrive(1, NT);
+          // The lanes' kept-list writes are ordered before lane 0's release.
+          __syncwarp();
+          BeamWsHeader* hdr = reinterpret_cast<BeamWsHeader*>(a.ws);
+          int last = 0;
+          if (tid == 0) {
+            hdr->status[row] = ST_OK;
+            hdr->count[row] = kept.n;
+            if (a.out_count) a.out_count[row] = kept.n;
+            last = atom_add_acq_rel_gpu(&hdr->counter, 1u) == (unsigned)(a.rows - 1);
+          }
+          last = __shfl_sync(0xffffffffu, last, 0);
+          bool block_merge = false;
+          if (last) {
+            block_merge = a.force_slow || !beam_merge_warp(a);
+            if (tid == 0 && !block_merge) atomicExch(&hdr->counter, 0u);
+          }
+          if (tid == 0) bs.flag = block_merge;
+        } else {
+          named_sync(1, NT);
+          kept.n = bs.flag2;
+          kept.M = bs.fval;
+          kept.tot = bs.u64a;
+        }
+      } else if (m <= 128) {
         if (tid < 32) {
           kept = m <= 64 ? warp_finish<2>(a, cv, ci, m, uu, &token, kidx, kval)
                          : warp_finish<4>(a, cv, ci, m, uu, &token, kidx, kval);
@@ -710,7 +791,8 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
         if (MODE == MODE_SAMPLE) token = draw_kept<NT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(regA));
       }
       const float Sf = fix_to_float(kept.tot);
-      for (int j = tid; j < kept.n; j += NT) {
+      const int first = published ? tid - 32 : tid, stride = published ? NT - 32 : NT;
+      for (int j = first < 0 ? kept.n : first; j < kept.n; j += stride) {
         const float p = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kept.M)), Sf);
         if (j < a.out_cap) {
           if (a.out_idx) a.out_idx[row * a.out_cap + j] = kidx[j];
@@ -766,6 +848,14 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
   }
   // Beam: publish this beam's kept list, then the last leader merges.
   BeamWsHeader* hdr = reinterpret_cast<BeamWsHeader*>(a.ws);
+  if (published) {
+    __syncthreads();  // warp 0's merge attempt is done
+    if (!bs.flag) return;
+    beam_merge(a, sh, regA);
+    __syncthreads();
+    if (tid == 0) atomicExch(&hdr->counter, 0u);
+    return;
+  }
   if (tid == 0) {
     hdr->status[row] = status;
     hdr->count[row] = kept.n;

@@ -180,3 +180,22 @@ def test_merge_mass_below_fixed_point(sv, lag, force):
     got, ref = run_both(sv, x, running, u, force=force)
     assert ref["n"] >= 2
     assert_same(got, ref)
+
+
+@pytest.mark.parametrize("force", [False, True], ids=["warp", "block"])
+@pytest.mark.parametrize("running,vocab,top_p,status", [
+    ([np.nan, 0.0], 300, 0.9, 1),      # NaN running score
+    ([np.inf, 0.0], 300, 0.9, 1),      # +inf + the -inf outside the kept list
+    ([-np.inf, -np.inf], 300, 0.9, 3),  # every score -inf
+    ([np.inf, 0.0], 50, 1.0, 2),       # every entry kept: a +inf score
+    ([-np.inf, 0.0], 300, 0.9, 0),     # one beam out of the draw
+])
+def test_nonfinite_running_scores(sv, running, vocab, top_p, status, force):
+    """Non-finite running scores give the statuses of the flattened softmax over
+    scores = log_probs + running (runtime_shared.py:231-233)."""
+    g = np.random.default_rng(vocab)
+    x = (2 * g.standard_normal((2, vocab))).astype(np.float32)
+    got, ref = run_both(sv, x, np.asarray(running, np.float32), g.random(4).astype(np.float32), p=top_p,
+                        force=force)
+    assert ref["status"] == status
+    assert_same(got, ref)
