@@ -393,8 +393,11 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-def graph_time_us(fn, reps=200):
-    """Mean device time of fn() replayed from a CUDA graph (after warm-up)."""
+def graph_time_us(fn, reps=40, per_graph=10):
+    """Mean device time of one fn() call, replayed from a CUDA graph that holds
+    per_graph calls back to back (after warm-up): a decode loop captures its
+    sampling step inside the step's graph, so the host's graph-launch gap is not
+    part of the step."""
     import torch
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -405,8 +408,9 @@ def graph_time_us(fn, reps=200):
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        fn()
-    for _ in range(10):
+        for _ in range(per_graph):
+            fn()
+    for _ in range(3):
         g.replay()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -415,7 +419,7 @@ def graph_time_us(fn, reps=200):
         g.replay()
     b.record()
     torch.cuda.synchronize()
-    return a.elapsed_time(b) * 1e3 / reps
+    return a.elapsed_time(b) * 1e3 / (reps * per_graph)
 
 
 def latency_extras(sv, dev):

@@ -200,15 +200,17 @@ __device__ void beam_merge(const RowArgs& a, Shared& sh, unsigned char* regA) {
         const int o = __ffs(bm) - 1;
         uint64_t w = 0;
         if (lane == o) {
+          // The whole segment without an early exit: its weights load together.
           uint64_t c = excl;
+#pragma unroll 8
           for (int e = e0; e < e1; ++e) {
-            c += W[e];
-            if (c > t) {
+            const uint64_t we = W[e];
+            c += we;
+            if (pick < 0 && c > t) {
               pick = e;
-              break;
+              w = we;
             }
           }
-          w = W[pick];
           mysum -= w;
           W[pick] = 0;
         }
@@ -439,6 +441,229 @@ __device__ bool beam_merge_warp(const RowArgs& a) {
     }
   }
   if (lane == 0) {
+    *a.out_npicks = n;
+    a.out_status[0] = ST_OK;
+  }
+  return true;
+}
+
+// The same merge spread over the block when a beam keeps more than its lanes of
+// one warp hold (eight beams of top-k 50): thread t holds beam b = t / (NT / B)
+// and slots (t % (NT / B)) * kMergeR .. + kMergeR - 1, so thread order then slot
+// order is again the flattened order.  Every input is requested in one round trip;
+// the reductions take one barrier each and every draw one.  Returns false, having
+// written nothing, when a beam keeps more entries than its threads hold.
+struct MergeShared {
+  float uni[64];
+  int stat[kMaxBeams];
+  int first_bad, flags, K;
+  float wmax[NT / 32];
+  unsigned long long wsum[NT / 32];
+  int wnz[NT / 32];
+  unsigned long long pick_w[2];
+  float fb_p[2][NT / 32];
+  int fb_e[2][NT / 32];
+};
+
+__device__ bool beam_merge_block(const RowArgs& a) {
+  __shared__ MergeShared m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = NT / 32;
+  const int B = a.rows;
+  const int TB = NT / B;  // threads per beam (B <= kMaxBeams)
+  const int b = tid / TB;
+  const bool act = b < B;
+  const bool lead = act && tid == b * TB;
+  const int j0 = (tid - b * TB) * kMergeR;
+  const BeamWsHeader* hdr = reinterpret_cast<const BeamWsHeader*>(a.ws);
+  const int* kidx0 = reinterpret_cast<const int*>(a.ws + sizeof(BeamWsHeader));
+  const float* kval0 = reinterpret_cast<const float*>(a.ws + sizeof(BeamWsHeader) + (size_t)B * a.ws_cap * 4);
+  const float NEG = Elem<float>::neg_inf();
+  int cnt = 0, stt = ST_OK;
+  float runb = 0.0f, uv = 0.0f;
+  float s[kMergeR];
+  int ki[kMergeR];
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) {
+    s[r] = 0.0f;
+    ki[r] = 0;
+  }
+  if (tid < a.npick) uv = ld_now(&a.uniforms[tid]);
+  if (act) {
+    cnt = ld_now(&hdr->count[b]);
+    stt = ld_now(&hdr->status[b]);
+    runb = ld_now(&a.running[b]);
+#pragma unroll
+    for (int r = 0; r < kMergeR; ++r) {
+      const int j = j0 + r;
+      if (j < a.ws_cap) {
+        s[r] = ld_now(&kval0[(size_t)b * a.ws_cap + j]);
+        ki[r] = ld_now(&kidx0[(size_t)b * a.ws_cap + j]);
+      }
+    }
+  }
+  if (tid == 0) {
+    m.first_bad = B;
+    m.flags = 0;
+    m.K = 0;
+  }
+  __syncthreads();
+  if (tid < a.npick) m.uni[tid] = uv;
+  if (lead) {
+    m.stat[b] = stt;
+    if (stt != ST_OK) atomicMin(&m.first_bad, b);
+    if (running_gives_nan(runb, cnt, a.vocab)) atomicOr(&m.flags, 2);
+    atomicAdd(&m.K, cnt);
+  }
+  if (act && cnt > TB * kMergeR) atomicOr(&m.flags, 1);
+  __syncthreads();
+  const int flags = m.flags;
+  if (flags & 1) return false;
+  const int st = m.first_bad < B ? m.stat[m.first_bad] : ((flags & 2) ? ST_NAN : ST_OK);
+  if (st != ST_OK || m.K == 0) {
+    if (tid == 0) {
+      *a.out_npicks = 0;
+      a.out_status[0] = st != ST_OK ? st : ST_ALLNEGINF;
+    }
+    return true;
+  }
+  unsigned valid = 0;
+  float mx = NEG;
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) {
+    const bool v = act && j0 + r < cnt;
+    valid |= (unsigned)v << r;
+    s[r] = __fadd_rn(s[r], runb);
+    if (v) mx = max_nan(mx, s[r]);
+  }
+  mx = warp_max_nan(mx);
+  if (lane == 0) m.wmax[warp] = mx;
+  __syncthreads();
+  float Ms = m.wmax[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) Ms = max_nan(Ms, m.wmax[w]);
+  if (Ms == __int_as_float(0x7f800000) || Ms == NEG) {
+    if (tid == 0) {
+      *a.out_npicks = 0;
+      a.out_status[0] = Ms > 0.0f ? ST_POSINF : ST_ALLNEGINF;
+    }
+    return true;
+  }
+  uint64_t W[kMergeR], excl[kMergeR];
+  float ex[kMergeR];
+  uint64_t lsum = 0;
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) {
+    ex[r] = ((valid >> r) & 1u) ? sv_exp(__fsub_rn(s[r], Ms)) : 0.0f;
+    W[r] = fixw(ex[r]);
+    excl[r] = lsum;
+    lsum += W[r];
+  }
+  const uint64_t lincl = warp_incl_scan_u64(lsum);
+  if (lane == 31) m.wsum[warp] = lincl;
+  __syncthreads();
+  uint64_t total = 0, wbase = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    const uint64_t v = m.wsum[w];
+    if (w < warp) wbase += v;
+    total += v;
+  }
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) excl[r] += wbase + lincl - lsum;
+  const float Sf = fix_to_float(total);
+  int nz = 0;
+#pragma unroll
+  for (int r = 0; r < kMergeR; ++r) {
+    const bool v = (valid >> r) & 1u;
+    const float p = __fdiv_rn(ex[r], Sf);
+    nz += __popc(__ballot_sync(0xffffffffu, v && p > 0.0f));
+    const int j = j0 + r;
+    if (v && a.out_prob && j < a.out_cap) a.out_prob[(size_t)b * a.out_cap + j] = p;
+  }
+  if (lane == 0) m.wnz[warp] = nz;
+  __syncthreads();
+  int nnz = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) nnz += m.wnz[w];
+  const int n = a.npick < nnz ? a.npick : nnz;
+  unsigned taken = 0;
+  for (int j = 0; j < n; ++j) {
+    const int q = j & 1;  // double-buffered: a slot is rewritten two draws later
+    int rs = -1;
+    if (total > 0) {
+      // The element whose fixed-point interval [excl, excl + W) holds
+      // floor(total * u); the elements after it lose its weight.
+      const uint64_t t = mulfloor(total, m.uni[j]);
+      uint64_t wl = 0;
+#pragma unroll
+      for (int r = 0; r < kMergeR; ++r)
+        if (excl[r] <= t && t - excl[r] < W[r]) {
+          wl = W[r];
+          rs = r;
+        }
+      if (rs >= 0) m.pick_w[q] = wl;
+      __syncthreads();
+      const uint64_t w = m.pick_w[q];
+#pragma unroll
+      for (int r = 0; r < kMergeR; ++r) {
+        if (excl[r] > t) excl[r] -= w;
+        if (r == rs) W[r] = 0;
+      }
+      total -= w;
+    } else {
+      // No fixed-point mass left: the largest remaining nonzero probability,
+      // ties to the lowest flattened position.
+      float best = -1.0f;
+      int be = 0x7fffffff;
+#pragma unroll
+      for (int r = 0; r < kMergeR; ++r) {
+        if (!((valid >> r) & 1u) || ((taken >> r) & 1u)) continue;
+        const float p = __fdiv_rn(ex[r], Sf);
+        if (p > 0.0f && p > best) {
+          best = p;
+          be = tid * kMergeR + r;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+        if (ob > best || (ob == best && oe < be)) {
+          best = ob;
+          be = oe;
+        }
+      }
+      if (lane == 0) {
+        m.fb_p[q][warp] = best;
+        m.fb_e[q][warp] = be;
+      }
+      __syncthreads();
+      best = m.fb_p[q][0];
+      be = m.fb_e[q][0];
+#pragma unroll
+      for (int w = 1; w < NW; ++w) {
+        const float ob = m.fb_p[q][w];
+        const int oe = m.fb_e[q][w];
+        if (ob > best || (ob == best && oe < be)) {
+          best = ob;
+          be = oe;
+        }
+      }
+      if (be / kMergeR == tid) rs = be - tid * kMergeR;
+    }
+    if (rs >= 0) {
+      // The pick's outputs from the owner's registers.
+#pragma unroll
+      for (int r = 0; r < kMergeR; ++r)
+        if (r == rs) {
+          taken |= 1u << r;
+          a.out_picks[j] = (int64_t)b * a.vocab + ki[r];
+          a.out_pick_scores[j] = s[r];
+        }
+    }
+  }
+  if (tid == 0) {
     *a.out_npicks = n;
     a.out_status[0] = ST_OK;
   }
@@ -851,7 +1076,7 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
   if (published) {
     __syncthreads();  // warp 0's merge attempt is done
     if (!bs.flag) return;
-    beam_merge(a, sh, regA);
+    if (a.force_slow || !beam_merge_block(a)) beam_merge(a, sh, regA);
     __syncthreads();
     if (tid == 0) atomicExch(&hdr->counter, 0u);
     return;
@@ -873,7 +1098,7 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
     if (tid == 0) bs.flag2 = done;
   }
   __syncthreads();
-  if (!bs.flag2) beam_merge(a, sh, regA);
+  if (!bs.flag2 && (a.force_slow || !beam_merge_block(a))) beam_merge(a, sh, regA);
   __syncthreads();
   if (tid == 0) atomicExch(&hdr->counter, 0u);
 }

@@ -199,3 +199,20 @@ def test_nonfinite_running_scores(sv, running, vocab, top_p, status, force):
                         force=force)
     assert ref["status"] == status
     assert_same(got, ref)
+
+
+@pytest.mark.parametrize("force", [False, True], ids=["regs", "block"])
+@pytest.mark.parametrize("beams,lag", [(8, 20.0), (8, 45.0), (5, 70.0), (16, 45.0)])
+def test_block_register_merge_mass_below_fixed_point(sv, beams, lag, force):
+    """Kept lists too long for the one-warp merge but within the block's register
+    slots, with beams far behind: draws past the fixed-point mass take the largest
+    remaining probability (runtime_shared.py:233-235)."""
+    g = np.random.default_rng(beams * 100 + int(lag))
+    x = (2 * g.standard_normal((beams, 4096))).astype(np.float32)
+    x[0, 17] += 40.0
+    running = np.array([0.0] + [-lag] * (beams - 1), np.float32)
+    u = g.random(2 * beams).astype(np.float32)
+    got, ref = run_both(sv, x, running, u, force=force)
+    counts = [int(np.isfinite(ref["logp"][b]).sum()) for b in range(beams)]
+    assert max(counts) > 4 * (32 // beams)  # past the one-warp merge
+    assert_same(got, ref)
