@@ -300,3 +300,20 @@ def test_cfg4_full_size_against_oracle(sv, path):
         assert got["token"][r] in got["idx"][r, :n]
         assert abs(got["prob"][r, :n].astype(np.float64).sum() - 1) < 1e-5
         assert np.all(np.diff(got["idx"][r, :n]) > 0)
+
+
+@pytest.mark.parametrize("vocab,dtype,dense", [(5000, torch.float32, True), (49152, torch.float16, False),
+                                               (12345, torch.bfloat16, True)])
+def test_stream_more_rows_than_ctas(sv, vocab, dtype, dense):
+    """More rows than the streaming kernel has resident CTAs, so CTAs work through
+    several rows each (the ring runs ahead across row boundaries); random settings,
+    bit-exact against the oracle."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    rows = 3 * sms + 7
+    g = np.random.default_rng(vocab)
+    x = (2 * g.standard_normal((rows, vocab))).astype(np.float32)
+    x[::5, g.choice(vocab, 12, replace=False)] += 9.0
+    u = g.random(rows).astype(np.float32)
+    ids = g.integers(0, vocab, (rows, 300))
+    got, ref = run_both(sv, x, u, ids=ids, T=1.3, p=0.85, dtype=dtype, dense=dense, cap=96, path="stream")
+    assert_same(got, ref, dense=dense)
