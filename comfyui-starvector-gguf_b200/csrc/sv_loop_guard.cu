@@ -6,7 +6,9 @@
 // each thread owns a contiguous run of window starts and rolls a polynomial hash
 // (mod 2^64, odd base) along it; a start whose hash equals the tail's hash is
 // verified token by token, so the verdict is exact.  The scan stops once
-// `repeats` occurrences are found.
+// `repeats` occurrences are found.  A chunk holds 16640 starts, so a 16K-token row
+// is staged once (16-byte vectors when the row is aligned); the rolling step
+// h(s+1) = h(s) B + (x[s+w] - x[s] B^w) keeps one multiply on the dependency chain.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -16,10 +18,28 @@
 namespace sv {
 
 constexpr int LG_NT = 256;
-constexpr int LG_PER = 17;                  // starts per thread (odd: no bank conflicts)
-constexpr int LG_CH = LG_NT * LG_PER;       // starts per chunk
+constexpr int LG_PER = 65;                  // starts per thread (odd: no bank conflicts)
+constexpr int LG_CH = LG_NT * LG_PER;       // starts per chunk (a 16K-token row in one)
 constexpr int LG_MAXW = 1024;               // window limit
 constexpr uint64_t LG_BASE = 0x9E3779B97F4A7C15ull;
+
+// The window hash sum_j p[j] B^(w-1-j) (mod 2^64) as four interleaved Horner
+// chains (j = k mod 4, step B^4), so its latency is a quarter of one chain's.
+template <typename Tok>
+__device__ __forceinline__ uint64_t hash_window(const Tok* p, int w) {
+  constexpr uint64_t B2 = LG_BASE * LG_BASE, B3 = B2 * LG_BASE, B4 = B2 * B2;
+  uint64_t h[4] = {0, 0, 0, 0};
+  int j = 0;
+  for (; j + 4 <= w; j += 4) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h[k] = h[k] * B4 + (uint64_t)(int64_t)p[j + k];
+  }
+  // Chain k holds p[k], p[k+4], ..., p[k+4(n-1)] with weights B^(4(n-1-i)); the full
+  // window weights them by B^(w-1-k-4i), i.e. B^(j-1-k) more for j = 4n.
+  uint64_t r = h[0] * B3 + h[1] * B2 + h[2] * LG_BASE + h[3];
+  for (; j < w; ++j) r = r * LG_BASE + (uint64_t)(int64_t)p[j];
+  return r;
+}
 
 template <typename Tok>
 __global__ void __launch_bounds__(LG_NT) loop_guard_kernel(const Tok* __restrict__ tokens, int64_t stride,
@@ -29,7 +49,6 @@ __global__ void __launch_bounds__(LG_NT) loop_guard_kernel(const Tok* __restrict
   Tok* buf = reinterpret_cast<Tok*>(lg_smem);                       // LG_CH + window - 1
   Tok* tail = buf + LG_CH + LG_MAXW;                                 // window
   __shared__ int count;
-  __shared__ unsigned long long htail, bpow;
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
   int64_t L = lengths[row];
@@ -41,36 +60,41 @@ __global__ void __launch_bounds__(LG_NT) loop_guard_kernel(const Tok* __restrict
   }
   for (int j = tid; j < window; j += LG_NT) tail[j] = t[L - window + j];
   if (tid == 0) count = 0;
-  __syncthreads();
-  if (tid == 0) {
-    uint64_t h = 0, p = 1;
-    for (int j = 0; j < window; ++j) {
-      h = h * LG_BASE + (uint64_t)(int64_t)tail[j];
-      if (j) p *= LG_BASE;
-    }
-    htail = h;
-    bpow = p;  // LG_BASE^(window-1)
-  }
-  __syncthreads();
-  const uint64_t ht = htail, bp = bpow;
+  // B^w: the rolling step h(s+1) = h(s) B + x[s+w] - x[s] B^w.
+  uint64_t bw = 1, bq = LG_BASE;
+  for (int e = window; e; e >>= 1, bq *= bq)
+    if (e & 1) bw *= bq;
+  // 16-byte vectors where the row allows them.
+  constexpr int VE = 16 / (int)sizeof(Tok);
+  const bool vec = (reinterpret_cast<uintptr_t>(t) & 15) == 0;
   const int64_t nstarts = L - window + 1;
+  uint64_t ht = 0;
   for (int64_t c0 = 0; c0 < nstarts; c0 += LG_CH) {
     const int64_t cn = nstarts - c0 < LG_CH ? nstarts - c0 : LG_CH;
     const int64_t ntok = cn + window - 1;
-    for (int64_t j = tid; j < ntok; j += LG_NT) buf[j] = t[c0 + j];
+    const Tok* src = t + c0;
+    if (vec) {
+      const int64_t nv = ntok / VE;
+      for (int64_t q = tid; q < nv; q += LG_NT)
+        reinterpret_cast<uint4*>(buf)[q] = reinterpret_cast<const uint4*>(src)[q];
+      for (int64_t j = nv * VE + tid; j < ntok; j += LG_NT) buf[j] = src[j];
+    } else {
+      for (int64_t j = tid; j < ntok; j += LG_NT) buf[j] = src[j];
+    }
     __syncthreads();
+    if (c0 == 0) ht = hash_window(tail, window);  // every thread, from shared memory
     const int s0 = tid * LG_PER;
     if (s0 < cn) {
-      uint64_t h = 0;
-      for (int j = 0; j < window; ++j) h = h * LG_BASE + (uint64_t)(int64_t)buf[s0 + j];
+      uint64_t h = hash_window(buf + s0, window);
       const int s1 = s0 + LG_PER < cn ? s0 + LG_PER : (int)cn;
       for (int s = s0; s < s1; ++s) {
-        if (s > s0) h = (h - (uint64_t)(int64_t)buf[s - 1] * bp) * LG_BASE + (uint64_t)(int64_t)buf[s + window - 1];
         if (h == ht) {
           bool eq = true;
           for (int j = 0; j < window && eq; ++j) eq = buf[s + j] == tail[j];
           if (eq) atomicAdd(&count, 1);
         }
+        if (s + 1 < s1)
+          h = h * LG_BASE + ((uint64_t)(int64_t)buf[s + window] - (uint64_t)(int64_t)buf[s] * bw);
       }
     }
     __syncthreads();
