@@ -4,8 +4,9 @@
 // occur at least `repeats` times (overlapping starts allowed, the tail itself
 // counted).  One CTA per row.  Tokens are staged chunk by chunk in shared memory;
 // each thread owns a contiguous run of window starts and rolls a polynomial hash
-// (mod 2^64, odd base) along it; a start whose hash equals the tail's hash is
-// verified token by token, so the verdict is exact.  The scan stops once
+// (mod 2^32, odd base, over a 32-bit mix of each token) along it; a start whose
+// hash equals the tail's hash is verified token by token, so the verdict is exact
+// (a hash collision costs one verification, never a wrong verdict).  The scan stops once
 // `repeats` occurrences are found.  A chunk holds 16640 starts, so a 16K-token row
 // is staged once (16-byte vectors when the row is aligned); the rolling step
 // h(s+1) = h(s) B + (x[s+w] - x[s] B^w) keeps one multiply on the dependency chain.
@@ -21,23 +22,27 @@ constexpr int LG_NT = 256;
 constexpr int LG_PER = 65;                  // starts per thread (odd: no bank conflicts)
 constexpr int LG_CH = LG_NT * LG_PER;       // starts per chunk (a 16K-token row in one)
 constexpr int LG_MAXW = 1024;               // window limit
-constexpr uint64_t LG_BASE = 0x9E3779B97F4A7C15ull;
+constexpr uint32_t LG_BASE = 0x9E3779B1u;
 
-// The window hash sum_j p[j] B^(w-1-j) (mod 2^64) as four interleaved Horner
+// A token as 32 bits for the hash (an int64 token folds its high half in).
+__device__ __forceinline__ uint32_t tok32(int32_t x) { return (uint32_t)x; }
+__device__ __forceinline__ uint32_t tok32(int64_t x) { return (uint32_t)x ^ ((uint32_t)(x >> 32) * 0x85EBCA6Bu); }
+
+// The window hash sum_j p[j] B^(w-1-j) (mod 2^32) as four interleaved Horner
 // chains (j = k mod 4, step B^4), so its latency is a quarter of one chain's.
 template <typename Tok>
-__device__ __forceinline__ uint64_t hash_window(const Tok* p, int w) {
-  constexpr uint64_t B2 = LG_BASE * LG_BASE, B3 = B2 * LG_BASE, B4 = B2 * B2;
-  uint64_t h[4] = {0, 0, 0, 0};
+__device__ __forceinline__ uint32_t hash_window(const Tok* p, int w) {
+  constexpr uint32_t B2 = LG_BASE * LG_BASE, B3 = B2 * LG_BASE, B4 = B2 * B2;
+  uint32_t h[4] = {0, 0, 0, 0};
   int j = 0;
   for (; j + 4 <= w; j += 4) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) h[k] = h[k] * B4 + (uint64_t)(int64_t)p[j + k];
+    for (int k = 0; k < 4; ++k) h[k] = h[k] * B4 + tok32(p[j + k]);
   }
-  // Chain k holds p[k], p[k+4], ..., p[k+4(n-1)] with weights B^(4(n-1-i)); the full
-  // window weights them by B^(w-1-k-4i), i.e. B^(j-1-k) more for j = 4n.
-  uint64_t r = h[0] * B3 + h[1] * B2 + h[2] * LG_BASE + h[3];
-  for (; j < w; ++j) r = r * LG_BASE + (uint64_t)(int64_t)p[j];
+  // Chain k holds p[k], p[k+4], ..., p[k+4(n-1)] with weights B^(4(n-1-i)); the
+  // window weights p[4i+k] by B^(4(n-1-i) + 3-k) for its first 4n tokens.
+  uint32_t r = h[0] * B3 + h[1] * B2 + h[2] * LG_BASE + h[3];
+  for (; j < w; ++j) r = r * LG_BASE + tok32(p[j]);
   return r;
 }
 
@@ -61,14 +66,14 @@ __global__ void __launch_bounds__(LG_NT) loop_guard_kernel(const Tok* __restrict
   for (int j = tid; j < window; j += LG_NT) tail[j] = t[L - window + j];
   if (tid == 0) count = 0;
   // B^w: the rolling step h(s+1) = h(s) B + x[s+w] - x[s] B^w.
-  uint64_t bw = 1, bq = LG_BASE;
+  uint32_t bw = 1, bq = LG_BASE;
   for (int e = window; e; e >>= 1, bq *= bq)
     if (e & 1) bw *= bq;
   // 16-byte vectors where the row allows them.
   constexpr int VE = 16 / (int)sizeof(Tok);
   const bool vec = (reinterpret_cast<uintptr_t>(t) & 15) == 0;
   const int64_t nstarts = L - window + 1;
-  uint64_t ht = 0;
+  uint32_t ht = 0;
   for (int64_t c0 = 0; c0 < nstarts; c0 += LG_CH) {
     const int64_t cn = nstarts - c0 < LG_CH ? nstarts - c0 : LG_CH;
     const int64_t ntok = cn + window - 1;
@@ -85,7 +90,7 @@ __global__ void __launch_bounds__(LG_NT) loop_guard_kernel(const Tok* __restrict
     if (c0 == 0) ht = hash_window(tail, window);  // every thread, from shared memory
     const int s0 = tid * LG_PER;
     if (s0 < cn) {
-      uint64_t h = hash_window(buf + s0, window);
+      uint32_t h = hash_window(buf + s0, window);
       const int s1 = s0 + LG_PER < cn ? s0 + LG_PER : (int)cn;
       for (int s = s0; s < s1; ++s) {
         if (h == ht) {
@@ -94,7 +99,7 @@ __global__ void __launch_bounds__(LG_NT) loop_guard_kernel(const Tok* __restrict
           if (eq) atomicAdd(&count, 1);
         }
         if (s + 1 < s1)
-          h = h * LG_BASE + ((uint64_t)(int64_t)buf[s + window] - (uint64_t)(int64_t)buf[s] * bw);
+          h = h * LG_BASE + (tok32(buf[s + window]) - tok32(buf[s]) * bw);
       }
     }
     __syncthreads();
