@@ -73,6 +73,8 @@ __host__ __device__ constexpr size_t smem_limit_stream() { return 232448; }
 
 size_t shared_static_bytes();
 cudaError_t launch_rows(const RowArgs& a, size_t smem_bytes, cudaStream_t stream);
+// The beam merge alone over kept lists in a.ws (a.rows beams, a.ws_cap entries each).
+cudaError_t launch_beam_merge(const RowArgs& a, cudaStream_t stream);
 size_t stream_smem_bytes(int64_t vocab);
 cudaError_t launch_stream(const RowArgs& a, size_t smem_bytes, cudaStream_t stream);
 

@@ -1103,6 +1103,21 @@ __global__ void __launch_bounds__(NT, 3) row_kernel(const RowArgs a) {
   if (tid == 0) atomicExch(&hdr->counter, 0u);
 }
 
+// The beam merge alone, over kept lists already in a workspace (the vocab-sharded
+// beam step): one CTA, the same cascade as the row kernel's last leader.
+__global__ void __launch_bounds__(NT) beam_merge_kernel(const RowArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Shared& sh = *reinterpret_cast<Shared*>(smem_raw);
+  unsigned char* regA = smem_raw + ((sizeof(Shared) + 127) & ~size_t(127));
+  const int tid = threadIdx.x;
+  if (tid < 32) {
+    const bool done = !a.force_slow && beam_merge_warp(a);
+    if (tid == 0) sh.bs.flag2 = done;
+  }
+  __syncthreads();
+  if (!sh.bs.flag2 && (a.force_slow || !beam_merge_block(a))) beam_merge(a, sh, regA);
+}
+
 // ---------------------------------------------------------------- host launch
 
 template <typename TIn, int MODE>
@@ -1148,6 +1163,15 @@ cudaError_t launch_t(const RowArgs& a, size_t smem, cudaStream_t stream) {
 }  // namespace
 
 size_t shared_static_bytes() { return (sizeof(Shared) + 127) & ~size_t(127); }
+
+// The merge's shared-memory staging (scores, weights and flattened ids of up to
+// 1024 entries) after the Shared block.
+constexpr size_t kMergeRegion = 16384;
+
+cudaError_t launch_beam_merge(const RowArgs& a, cudaStream_t stream) {
+  beam_merge_kernel<<<1, NT, shared_static_bytes() + kMergeRegion, stream>>>(a);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_rows(const RowArgs& a, size_t smem, cudaStream_t stream) {
   if (a.mode == MODE_SAMPLE) {

@@ -294,3 +294,96 @@ def pack_slice(local, offset, capacity, out):
                                _stream(out.device))
     L.check(rc, "sv_pack_slice")
     return out
+
+
+def beam_slice_stats(logits_slice, global_max=None):
+    """One rank's slice statistics for the vocab-sharded beam step
+    (sv_beam_slice_stats).  Without global_max: {"max": float [beams], "flags":
+    int32 [beams]} (2 NaN, 1 +inf, 0 neither), to all-reduce with MAX.  With the
+    reduced maxima: {"sum": int64 [beams]}, the exact fixed-point exp sums, to
+    all-reduce with SUM."""
+    x = _rows(logits_slice)
+    B, W = x.shape
+    dev = x.device
+    stride = x.stride(0) if B > 1 else 0
+    if global_max is None:
+        mx = torch.empty(B, dtype=torch.float32, device=dev)
+        fl = torch.empty(B, dtype=torch.int32, device=dev)
+        rc = L.lib().sv_beam_slice_stats(x.data_ptr(), _DTYPES[x.dtype], B, W, stride, None, mx.data_ptr(),
+                                         fl.data_ptr(), None, _stream(dev))
+        L.check(rc, "sv_beam_slice_stats")
+        return {"max": mx, "flags": fl}
+    gm = global_max.reshape(-1)
+    _need_cuda(gm, "global_max")
+    if gm.dtype != torch.float32 or not gm.is_contiguous() or gm.numel() != B:
+        raise ValueError("global_max must be a contiguous float32 tensor [beams]")
+    sm = torch.empty(B, dtype=torch.int64, device=dev)
+    rc = L.lib().sv_beam_slice_stats(x.data_ptr(), _DTYPES[x.dtype], B, W, stride, gm.data_ptr(), None, None,
+                                     sm.data_ptr(), _stream(dev))
+    L.check(rc, "sv_beam_slice_stats")
+    return {"sum": sm}
+
+
+def beam_slice_logprobs(logits_slice, global_max, global_sum, out=None):
+    """The slice's log_softmax (x - M) - ln(S 2^-44), float32 [beams, width], from the
+    all-reduced statistics (sv_beam_slice_logprobs)."""
+    x = _rows(logits_slice)
+    B, W = x.shape
+    dev = x.device
+    gm, gs = global_max.reshape(-1), global_sum.reshape(-1)
+    for t, n, dt in ((gm, "global_max", torch.float32), (gs, "global_sum", torch.int64)):
+        _need_cuda(t, n)
+        if t.dtype != dt or not t.is_contiguous() or t.numel() != B:
+            raise ValueError(f"{n} must be a contiguous {dt} tensor [beams]")
+    o = out if out is not None else torch.empty((B, W), dtype=torch.float32, device=dev)
+    rc = L.lib().sv_beam_slice_logprobs(x.data_ptr(), _DTYPES[x.dtype], B, W, x.stride(0) if B > 1 else 0,
+                                        gm.data_ptr(), gs.data_ptr(), o.data_ptr(), o.stride(0) if B > 1 else 0,
+                                        _stream(dev))
+    L.check(rc, "sv_beam_slice_logprobs")
+    return o
+
+
+def merge_beam_shards(packed, global_max, global_flags, running_scores, uniforms, *, capacity, vocab, top_p=0.9,
+                      top_k=50, keep=2, num_picks=None, out_capacity=0, workspace=None, out=None):
+    """Merge side of the vocab-sharded beam step (sv_merge_beam_shards): packed int32
+    [shards, beams, 2 * capacity + 2].  Returns beam_step's dict (picks, scores, n,
+    status, and the per-beam kept lists when out_capacity > 0)."""
+    _need_cuda(packed, "packed")
+    if packed.dtype != torch.int32 or packed.dim() != 3 or not packed.is_contiguous():
+        raise ValueError("packed must be a contiguous int32 tensor [shards, beams, 2 * capacity + 2]")
+    S, B, Wd = packed.shape
+    if Wd != 2 * capacity + 2:
+        raise ValueError("packed records must hold 2 * capacity + 2 values")
+    P = 2 * B if num_picks is None else int(num_picks)
+    dev = packed.device
+    rs, u = running_scores.reshape(-1), uniforms.reshape(-1)
+    for t, n, size in ((rs, "running_scores", B), (u, "uniforms", P)):
+        _need_cuda(t, n)
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < size:
+            raise ValueError(f"{n} must be a contiguous float32 tensor with {size} values")
+    gm, gf = global_max.reshape(-1), global_flags.reshape(-1)
+    if gm.dtype != torch.float32 or gf.dtype != torch.int32 or gm.numel() != B or gf.numel() != B:
+        raise ValueError("global_max float32 [beams] and global_flags int32 [beams]")
+    o = out if out is not None else {}
+    need = {"picks": lambda: torch.full((P,), -1, dtype=torch.int64, device=dev),
+            "scores": lambda: torch.zeros(P, dtype=torch.float32, device=dev),
+            "n": lambda: torch.zeros(1, dtype=torch.int32, device=dev),
+            "status": lambda: torch.zeros(1, dtype=torch.int32, device=dev)}
+    if out_capacity:
+        need.update(kept_count=lambda: torch.zeros(B, dtype=torch.int32, device=dev),
+                    kept_idx=lambda: torch.full((B, out_capacity), -1, dtype=torch.int32, device=dev),
+                    kept_logprob=lambda: torch.zeros((B, out_capacity), dtype=torch.float32, device=dev),
+                    kept_prob=lambda: torch.zeros((B, out_capacity), dtype=torch.float32, device=dev))
+    for k, make in need.items():
+        if k not in o:
+            o[k] = make()
+    nbytes = L.lib().sv_merge_beam_shards_workspace_bytes(B, S, int(capacity))
+    ws = workspace if workspace is not None else torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    rc = L.lib().sv_merge_beam_shards(
+        packed.data_ptr(), S, B, int(capacity), int(vocab), gm.data_ptr(), gf.data_ptr(), rs.data_ptr(),
+        u.data_ptr(), P, float(top_p), int(top_k), int(keep), ws.data_ptr(), ws.numel(), o["picks"].data_ptr(),
+        o["scores"].data_ptr(), o["n"].data_ptr(), o["status"].data_ptr(), _ptr(o.get("kept_count")),
+        _ptr(o.get("kept_idx")), _ptr(o.get("kept_logprob")), _ptr(o.get("kept_prob")), int(out_capacity),
+        _stream(dev))
+    L.check(rc, "sv_merge_beam_shards")
+    return o

@@ -99,3 +99,37 @@ def sample_step_vocab_sharded(shard_logits, uniforms, *, offset, seen_bits=None,
     packed = all_gather_records(pack_slice(local, offset, capacity), group)
     return (merge_fn or ops.merge_shards)(packed, uniforms, capacity=capacity, top_p=top_p, top_k=top_k, keep=keep,
                                           out_capacity=out_capacity, out=out)
+
+
+def beam_step_vocab_sharded(shard_logits, running_scores, uniforms, *, offset, vocab, seen_bits=None, seen=None,
+                            temperature=1.5, top_p=0.9, top_k=50, keep=2, repetition_penalty=3.1, capacity=64,
+                            num_picks=None, out_capacity=0, group=None, stats_fn=None, logprob_fn=None,
+                            step_fn=None, merge_fn=None, out=None):
+    """The vocab-sharded beam step (runtime_shared.py:230-235), called by every rank
+    of `group` with its slice [beams, width] of every beam's logits at `offset`.
+
+    Three exchanges: the slices' maxima and NaN / +inf flags (all-reduce MAX), their
+    exact fixed-point exp sums against the global maximum (all-reduce SUM, int64),
+    then the slices' kept lists (all-gather).  Between them each rank forms its
+    slice's log_softmax and runs the slice step on it (penalty, temperature, the
+    slice's top-k with ties; top-p off).  Every rank returns beam_step's dict for
+    the whole rows (picks are beam * vocab + token).  stats_fn / logprob_fn /
+    step_fn / merge_fn replace the CUDA calls (the tests run the exchange on CPU
+    ranks with them).
+    """
+    B = shard_logits.shape[0]
+    stats = stats_fn or ops.beam_slice_stats
+    first = stats(shard_logits)
+    gmax, gflags = first["max"].clone(), first["flags"].clone()
+    dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=group)
+    dist.all_reduce(gflags, op=dist.ReduceOp.MAX, group=group)
+    gsum = stats(shard_logits, global_max=gmax)["sum"].clone()
+    dist.all_reduce(gsum, op=dist.ReduceOp.SUM, group=group)
+    lp = (logprob_fn or ops.beam_slice_logprobs)(shard_logits, gmax, gsum)
+    dummy = torch.zeros(B, dtype=torch.float32, device=lp.device)
+    local = (step_fn or slice_step)(lp, dummy, offset=offset, seen_bits=seen_bits, seen=seen, temperature=temperature,
+                                    top_k=top_k, keep=keep, repetition_penalty=repetition_penalty, capacity=capacity)
+    packed = all_gather_records(pack_slice(local, offset, capacity), group)
+    return (merge_fn or ops.merge_beam_shards)(packed, gmax, gflags, running_scores, uniforms, capacity=capacity,
+                                               vocab=vocab, top_p=top_p, top_k=top_k, keep=keep,
+                                               num_picks=num_picks, out_capacity=out_capacity, out=out)

@@ -217,6 +217,46 @@ int sv_merge_shards(const int32_t* packed, int32_t shards, int32_t rows, int32_t
 int sv_pack_slice(const int32_t* count, const int32_t* status, const int32_t* idx, const float* score, int32_t rows,
                   int32_t capacity, int32_t offset, int32_t* out_records, void* stream);
 
+/*
+ * Vocab-sharded beam step.  No counterpart in the reference (it has no sharded
+ * vocabulary); together these replace runtime_shared.py:230-235 for beams whose
+ * vocabulary is split across ranks.  Each rank owns the same slice of every
+ * beam's row:
+ *   1. sv_beam_slice_stats with global_max = NULL: out_max [beams] the slice's
+ *      maximum (NaN-propagating), out_flags [beams] 2 for a NaN in the slice, else
+ *      1 for a +inf, else 0.  The ranks all-reduce both with MAX.
+ *   2. sv_beam_slice_stats with global_max = the reduced maxima: out_sum [beams]
+ *      the slice's exact sum of trunc(exp(x - M) * 2^44).  The ranks all-reduce it
+ *      with SUM (int64: the sum wraps the same on every rank).
+ *   3. sv_beam_slice_logprobs: the slice's log_softmax (x - M) - ln(sum * 2^-44),
+ *      float32 [beams, out_row_stride], as sv_beam_step forms it.
+ *   4. sv_sample_step on those log-probs with top_p = 1, keep = 2 and out_capacity
+ *      = capacity (penalty, temperature and the slice's top-k with ties), then
+ *      sv_pack_slice; the ranks all-gather the records.
+ *   5. sv_merge_beam_shards: per beam the exact top-k with ties and top-p over the
+ *      union, then + running scores, the softmax over all beams' kept entries,
+ *      count_nonzero and the draws without replacement, as sv_beam_step.  Results
+ *      equal sv_beam_step on the whole rows.  global_max / global_flags are the
+ *      reduced statistics of step 1 (they carry the log_softmax stage's status);
+ *      vocab is the whole row's size (picks are beam * vocab + token); workspace
+ *      holds sv_merge_beam_shards_workspace_bytes(beams, shards, capacity) bytes,
+ *      16-byte aligned (no zero-fill needed).  Outputs as sv_beam_step.
+ * logits [beams, slice_len] at logits_row_stride elements; beams <= 32.
+ */
+int sv_beam_slice_stats(const void* logits, int32_t logits_dtype, int32_t beams, int32_t slice_len,
+                        int64_t logits_row_stride, const float* global_max, float* out_max, int32_t* out_flags,
+                        uint64_t* out_sum, void* stream);
+int sv_beam_slice_logprobs(const void* logits, int32_t logits_dtype, int32_t beams, int32_t slice_len,
+                           int64_t logits_row_stride, const float* global_max, const uint64_t* global_sum, float* out,
+                           int64_t out_row_stride, void* stream);
+size_t sv_merge_beam_shards_workspace_bytes(int32_t beams, int32_t shards, int32_t capacity);
+int sv_merge_beam_shards(const int32_t* packed, int32_t shards, int32_t beams, int32_t capacity, int32_t vocab,
+                         const float* global_max, const int32_t* global_flags, const float* running_scores,
+                         const float* uniforms, int32_t num_picks, double top_p, int32_t top_k, int32_t keep,
+                         void* workspace, size_t workspace_bytes, int64_t* out_picks, float* out_pick_scores,
+                         int32_t* out_num_picks, int32_t* out_status, int32_t* out_kept_count, int32_t* out_kept_idx,
+                         float* out_kept_logprob, float* out_kept_prob, int32_t out_capacity, void* stream);
+
 /* Text of a return or status code. */
 const char* sv_error_string(int32_t code);
 

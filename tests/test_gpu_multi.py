@@ -1,4 +1,4 @@
-"""The vocab-sharded sample step across GPUs: one process per GPU, NCCL all-gather.
+"""The vocab-sharded sample and beam steps across GPUs: one process per GPU, NCCL.
 
 Runs only on a box with at least 2 GPUs (skipped otherwise).  Each rank holds one
 slice of the vocabulary; every rank's merged tokens, kept sets and probabilities
@@ -84,3 +84,75 @@ def test_vocab_sharded_across_gpus():
             n = min(int(ref["count"][r]), CAP)
             np.testing.assert_array_equal(g["idx"][r, :n], ref["idx"][r, :n])
             np.testing.assert_array_equal(g["prob"][r, :n], ref["prob"][r, :n])
+
+
+BEAMS = 4
+
+
+def _beam_data():
+    g = np.random.default_rng(43)
+    x = (2.5 * g.standard_normal((BEAMS, V))).astype(np.float32)
+    seen = np.zeros((BEAMS, V), bool)
+    seen[np.arange(BEAMS)[:, None], g.integers(0, V, (BEAMS, 2048))] = True
+    running = np.array([-1.0, -4.0, -2.5, -30.0], np.float32)
+    u = g.random(2 * BEAMS).astype(np.float32)
+    return x, seen, running, u
+
+
+def _beam_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        import __graft_entry__
+        sv = __graft_entry__.load_package()
+        x, seen, running, u = _beam_data()
+        w = V // world
+        off = rank * w
+        packed = np.packbits(seen, axis=1, bitorder="little")
+        bits = torch.from_numpy(np.ascontiguousarray(packed).view(np.int32)).to(dev)
+        out = sv.sharded.beam_step_vocab_sharded(
+            torch.from_numpy(np.ascontiguousarray(x[:, off:off + w])).to(dev), torch.from_numpy(running).to(dev),
+            torch.from_numpy(u).to(dev), offset=off, vocab=V, seen_bits=bits, capacity=CAP, out_capacity=CAP)
+        torch.cuda.synchronize()
+        q.put((rank, {k: v.cpu().numpy() for k, v in out.items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocab_sharded_beam_step_across_gpus():
+    """The beam step with every beam's vocabulary split across the GPUs: two
+    all-reduces (the log_softmax statistics) and one all-gather."""
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(world, 8)
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_beam_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    x, seen, running, u = _beam_data()
+    ref = O.beam(x, running, u, seen=seen.astype(np.uint8), temperature=1.5, top_p=0.9, top_k=50, keep=2,
+                 npick=2 * BEAMS)
+    for rank in range(world):
+        g = got[rank]
+        assert int(g["status"][0]) == ref["status"] == 0
+        n = int(g["n"][0])
+        assert n == ref["n"]
+        np.testing.assert_array_equal(g["picks"][:n], ref["picks"])
+        np.testing.assert_array_equal(g["scores"][:n], ref["scores"])
+        for b in range(BEAMS):
+            ki = np.nonzero(np.isfinite(ref["logp"][b]))[0]
+            assert g["kept_count"][b] == len(ki)
+            k = min(len(ki), CAP)
+            np.testing.assert_array_equal(g["kept_idx"][b, :k], ki[:k])
+            np.testing.assert_array_equal(g["kept_logprob"][b, :k], ref["logp"][b][ki[:k]])
