@@ -93,39 +93,60 @@ class _TokenHistory:
         torch.index_select(self.ids, 0, parents, out=self.spare)
         self.ids, self.spare = self.spare, self.ids
 
-    def repeating(self, row=0):
-        if self.length < LOOP_WINDOW * LOOP_REPEATS:
+    def repeating(self, row=0, length=None):
+        length = self.length if length is None else length
+        if length < LOOP_WINDOW * LOOP_REPEATS:
             return False
-        lengths = torch.full((1,), self.length, dtype=torch.int32, device=self.ids.device)
+        lengths = torch.full((1,), length, dtype=torch.int32, device=self.ids.device)
         return bool(ops.loop_guard(self.ids[row:row + 1], lengths, LOOP_WINDOW, LOOP_REPEATS)[0])
+
+
+# The host reads the sampled tokens once per loop-guard period (runtime_shared.py:207)
+# instead of once per token.
+_SYNC_EVERY = 16
 
 
 def _sample(decoder, embeddings, max_new_tokens, temperature, top_p, stop_ids, eos_id, loop_guard, on_step,
             uniforms=None):
-    """Transformers' multinomial sampling of one sequence (runtime_shared.py:194-211)."""
+    """Transformers' multinomial sampling of one sequence (runtime_shared.py:194-211).
+
+    The tokens stay on the device: the host reads them (and the steps' statuses) once
+    every 16 steps and at the last step, then goes through that block's steps in
+    order - the status check, the progress callback, the end check and, every 16th
+    step, the loop guard - exactly as the reference does per token, so the tokens,
+    the stop reason, the callbacks and the errors are the reference's.  Up to 15
+    decode steps issued after an end inside a block are discarded.
+    """
     decoding, logits = decoder.prefill(embeddings, 1, embeddings.shape[1] + max_new_tokens)
     device, vocab = logits.device, logits.shape[-1]
     if uniforms is None:
         uniforms = torch.rand((max_new_tokens, 1), dtype=torch.float32, device=device)
     seen = ops.seen_bitmap(1, vocab, device)
     history = _TokenHistory(1, max_new_tokens, device)
+    statuses = torch.zeros(max_new_tokens, dtype=torch.int32, device=device)
     out = {}
     tokens = []
+    synced = 0
     for step in range(max_new_tokens):
+        out["status"] = statuses[step:step + 1]  # the kernel writes each step's status in place
         out = ops.sample_step(logits.reshape(1, vocab), uniforms[step], seen_bits=seen, temperature=temperature,
                               top_p=top_p, top_k=TOP_K, keep=1, repetition_penalty=REPETITION_PENALTY,
                               update_seen_bits=seen, out=out)
         token = out["token"]
         history.append(token)
-        value = int(token)
-        if value < 0:
-            _raise_status(int(out["status"][0]))
-        tokens.append(value)
-        on_step(step + 1)
-        if _ends(tokens, stop_ids, eos_id):
-            return tokens, 'stop'
-        if loop_guard and step % 16 == 15 and history.repeating():
-            return tokens, 'repetition'
+        if step % _SYNC_EVERY == _SYNC_EVERY - 1 or step + 1 == max_new_tokens:
+            block = history.ids[0, synced:step + 1].tolist()
+            block_status = statuses[synced:step + 1].tolist()
+            for j, (value, status) in enumerate(zip(block, block_status), start=synced):
+                if value < 0:
+                    _raise_status(int(status))
+                tokens.append(value)
+                on_step(j + 1)
+                if _ends(tokens, stop_ids, eos_id):
+                    return tokens, 'stop'
+                if loop_guard and j % 16 == 15 and history.repeating(length=j + 1):
+                    return tokens, 'repetition'
+            synced = step + 1
         if step + 1 < max_new_tokens:
             logits = decoding.step(token)
     return tokens, 'token_limit'

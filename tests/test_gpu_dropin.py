@@ -122,3 +122,32 @@ def test_repeating_matches_reference_rule(rs):
     assert not rs._repeating(script[:191])
     assert rs._repeating(script[:192])
     assert not rs._repeating(list(range(300)))
+
+
+def test_stop_inside_a_read_block(rs):
+    """The host reads sampled tokens once per 16 steps: an end at step 21 still
+    stops there, with the progress callback called once per step up to it."""
+    events = []
+    script = [7] * 19 + [3, 4] + [8] * 20
+    svg = rs.generate_tokens(CudaScriptDecoder(script), TinyTokenizer(), torch.zeros(1, 8, 4, device=DEV),
+                             max_new_tokens=30, num_beams=1, progress_callback=events.append)
+    assert svg == "<svg" + " 7" * 19 + " 3 4"
+    assert events == list(range(1, 22))
+
+
+class NanAtStepDecoder(CudaScriptDecoder):
+    def _logits(self, rows):
+        logits = super()._logits(rows)
+        if self.step_index == 9:
+            logits[:, 5] = float("nan")
+        return logits
+
+
+def test_error_status_inside_a_read_block(rs):
+    """A step whose logits hold a NaN raises the reference's error even though the
+    host reads the steps' statuses only once per 16 steps."""
+    events = []
+    with pytest.raises(RuntimeError, match="probability tensor contains"):
+        rs.generate_tokens(NanAtStepDecoder([7]), TinyTokenizer(), torch.zeros(1, 8, 4, device=DEV),
+                           max_new_tokens=30, num_beams=1, progress_callback=events.append)
+    assert events == list(range(1, 10))
