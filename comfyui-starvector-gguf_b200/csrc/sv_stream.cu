@@ -480,8 +480,10 @@ __global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a
       }
       // The bound warp publishes a bound from the bins as they stand, before the
       // barrier so that its latency overlaps the other warps' passes (counts only
-      // grow, so a partial histogram gives a valid, lower bound).
-      if (warp == kBoundWarp) {
+      // grow, so a partial histogram gives a valid, lower bound).  Every fourth
+      // chunk only: the scan sits on each chunk's critical path, and a bound a few
+      // chunks older keeps a few more units.
+      if (warp == kBoundWarp && (c & 3) == 3) {
         __syncwarp();
         const float tb = hist_bound(sh.bins, base_key, bin_shift, kk, T);
         if (lane == 0) sh.te_pub = fmaxf(sh.te_pub, tb);
