@@ -367,6 +367,7 @@ def run_ours(args, rank, world, local_rank):
     extras = latency_extras(sv, dev) if rank == 0 and not args.no_extras else {}
     if world > 1 and not args.no_extras:
         extras.update(vocab_sharded_extra(sv, dev, rank, world))  # every rank takes part
+        extras.update(vocab_sharded_beam_extra(sv, dev, rank, world))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         rps, rows, dt = cpu_port_rows_per_s(sets[0]["host"], seconds=args.cpu_seconds)
@@ -490,6 +491,44 @@ def vocab_sharded_extra(sv, dev, rank, world, steps=20, warmup=3):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return {"cfg5_vocab_sharded_us_per_step": float(t[0]), "cfg5_vocab_sharded_slices": world,
             "cfg5_vocab_sharded_max_status": int(t[1])}
+
+
+def vocab_sharded_beam_extra(sv, dev, rank, world, steps=20, warmup=3):
+    """Config 3's beam step with every beam's vocabulary split across the ranks
+    (slice statistics, two NCCL all-reduces, slice step, one all-gather, merge).
+    Device time per step, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    d = cfg3()
+    beams, cap = d["logits"].shape[0], 64
+    w = V // world
+    off = rank * w
+    xd = torch.from_numpy(np.ascontiguousarray(d["logits"][:, off:off + w])).to(dev).to(torch.bfloat16)
+    seen = np.zeros((beams, V), bool)
+    seen[np.arange(beams)[:, None], d["history"]] = True
+    packed = np.packbits(seen, axis=1, bitorder="little")
+    bits = torch.from_numpy(np.ascontiguousarray(packed).view(np.int32)).to(dev)
+    rs = torch.from_numpy(d["running"]).to(dev)
+    ud = torch.from_numpy(d["uniforms"]).to(dev)
+    out = {}
+
+    def step():
+        sv.sharded.beam_step_vocab_sharded(xd, rs, ud, offset=off, vocab=V, seen_bits=bits, capacity=cap, out=out)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    bad = int(out["status"].max().item())
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) * 1e3 / steps, float(bad)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"cfg3_vocab_sharded_beam_us_per_step": float(t[0]), "cfg3_vocab_sharded_beam_max_status": int(t[1])}
 
 
 def main():
