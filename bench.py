@@ -210,9 +210,10 @@ def profiled_traffic():
     return None
 
 
-def cpu_port_rows_per_s(data, seconds=10.0, chunk=64):
-    """The CPU port of the reference algorithm (oracle/) on all host threads, on a
-    bounded sample: chunks of `chunk` rows of the workload until `seconds` pass."""
+def cpu_port_rows_per_s(data, seconds=10.0, chunk=64, threads=0):
+    """The CPU port of the reference algorithm (oracle/) on all host threads (or
+    `threads`), on a bounded sample: chunks of `chunk` rows of the workload until
+    `seconds` pass."""
     from oracle import oracle as O
     x, h, u = data["logits"], data["history"], data["uniforms"]
     n = x.shape[0]
@@ -221,7 +222,7 @@ def cpu_port_rows_per_s(data, seconds=10.0, chunk=64):
     i = 0
     while True:
         s = slice(i, i + chunk)
-        O.sample(x[s], u[s], ids=h[s], temperature=1.5, top_p=0.9, cap=0)
+        O.sample(x[s], u[s], ids=h[s], temperature=1.5, top_p=0.9, cap=0, threads=threads)
         rows += x[s].shape[0]
         i = (i + chunk) % n
         if time.perf_counter() - t0 >= seconds:
@@ -373,6 +374,10 @@ def run_ours(args, rank, world, local_rank):
         rps, rows, dt = cpu_port_rows_per_s(sets[0]["host"], seconds=args.cpu_seconds)
         cpu = {"value": rps, "unit": "rows/s", "cores": os.cpu_count(), "kind": "port",
                "sample": f"{rows} rows of the workload in {dt:.1f} s (oracle/ C port, OpenMP over rows)"}
+        rps1, rows1, dt1 = cpu_port_rows_per_s(sets[0]["host"], seconds=min(args.cpu_seconds, 5.0), chunk=8,
+                                               threads=1)
+        cpu["single_thread"] = {"value": rps1, "unit": "rows/s", "cores": 1,
+                                "sample": f"{rows1} rows in {dt1:.1f} s on one thread"}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
