@@ -377,8 +377,13 @@ def merge_beam_shards(packed, global_max, global_flags, running_scores, uniforms
     for k, make in need.items():
         if k not in o:
             o[k] = make()
-    nbytes = L.lib().sv_merge_beam_shards_workspace_bytes(B, S, int(capacity))
-    ws = workspace if workspace is not None else torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    ws = workspace
+    if ws is None:
+        key = ("merge_beam", dev.index, _stream(dev), B, S, int(capacity))
+        ws = _WORKSPACES.get(key)
+        if ws is None:
+            nbytes = L.lib().sv_merge_beam_shards_workspace_bytes(B, S, int(capacity))
+            ws = _WORKSPACES[key] = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     rc = L.lib().sv_merge_beam_shards(
         packed.data_ptr(), S, B, int(capacity), int(vocab), gm.data_ptr(), gf.data_ptr(), rs.data_ptr(),
         u.data_ptr(), P, float(top_p), int(top_k), int(keep), ws.data_ptr(), ws.numel(), o["picks"].data_ptr(),

@@ -119,11 +119,11 @@ def beam_step_vocab_sharded(shard_logits, running_scores, uniforms, *, offset, v
     """
     B = shard_logits.shape[0]
     stats = stats_fn or ops.beam_slice_stats
-    first = stats(shard_logits)
-    gmax, gflags = first["max"].clone(), first["flags"].clone()
+    first = stats(shard_logits)  # fresh tensors: reduced in place
+    gmax, gflags = first["max"], first["flags"]
     dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=group)
     dist.all_reduce(gflags, op=dist.ReduceOp.MAX, group=group)
-    gsum = stats(shard_logits, global_max=gmax)["sum"].clone()
+    gsum = stats(shard_logits, global_max=gmax)["sum"]
     dist.all_reduce(gsum, op=dist.ReduceOp.SUM, group=group)
     lp = (logprob_fn or ops.beam_slice_logprobs)(shard_logits, gmax, gsum)
     dummy = torch.zeros(B, dtype=torch.float32, device=lp.device)
