@@ -1,33 +1,38 @@
-// sv_stream.cu -- the streaming row kernel (sm_100a): many independent rows.
+// sv_stream.cu -- the batched row kernel (sm_100a): many independent rows.
 //
-// Persistent CTAs work through their rows one at a time.  A row's
-// logits (and, ahead of them, its history ids) stream through a per-CTA ring of
-// shared-memory slots filled by TMA bulk copies (cp.async.bulk, one mbarrier per
-// slot); the ring runs ahead across row boundaries, so HBM keeps streaming while
-// the CTA computes or finishes a row.
+// One CTA per row.  The row's logits stream straight into registers as 32-byte
+// units (256-bit non-caching loads; BU units per thread per batch, the CTA's batch
+// a contiguous NT*BU*32-byte span) through two register buffers used in turn, so
+// the next batch is always in flight while a warp works on the current one.
+// Nothing is staged in shared memory and no block barrier separates the batches.
 //
 // Per row (runtime_shared.py:200-202):
-//   1. the row's seen bitmap in shared memory, from the history;
-//   2. per chunk, one pass over 16-byte units: the unit maximum of the raw scores
-//      is tested against the current lower bound tau of the row's k-th largest
-//      penalised score, and the units that reach it are kept (their 16 bytes and
-//      seen bits).  The units also feed 128 lane-pair group values, a unit with a
-//      seen token through a lower bound of its penalised maximum (each group value
-//      is at or below a distinct element of its group, so the k-th largest group
-//      value bounds the row's k-th largest from below).  In the first chunk the
-//      exact k-th largest of the chunk's group values gives the first bound;
-//      later group values go into a 256-bin histogram over ordered float keys,
-//      whose highest bin edge with at least k values at or above it is a
-//      tightening bound;
-//   3. finish: the kept units' elements whose penalised score (:172-173) reaches
-//      the final bound are the candidates, tempered (:178-179); then the exact
-//      k-th largest with ties (:180-181), top-p over the ascending (value, index)
-//      order with exact fixed-point mass (:182-186) and the draw from the row's
-//      uniform, by one warp for up to 64 candidates.  A row with too many (huge tie
-//      groups) takes the general path over the whole row.
+//   1. the row's seen bitmap in shared memory, from the history (its ids loaded
+//      in one round while the first two batches of logits are prefetched into L2);
+//   2. a first lower bound tau of the row's k-th largest penalised score: the
+//      exact k-th largest of the threads' maxima over the unseen elements of the
+//      first two batches (NT distinct elements, each at or below its penalised
+//      score);
+//   3. every batch: the unit maxima of the raw scores (the penalty never raises a
+//      score, so a unit below tau holds no candidate) and, for the rare units that
+//      reach tau, each element's penalised score (:172-173, the seen bit looked up
+//      only here).  Those reaching tau are appended to the warp's own candidate
+//      list (ballot-aggregated, no shared counter) and counted in a 256-bin
+//      histogram over ordered float keys shared by the CTA.  A warp whose list grew
+//      by RW entries recomputes the bound from the histogram (the highest bin edge
+//      with at least k counted values at or above it: counts only grow, so any
+//      snapshot gives a valid bound) and raises the shared tau;
+//   4. finish: the candidates reaching the final bound, tempered (:178-179); the
+//      exact k-th largest with ties (:180-181), top-p over the ascending (value,
+//      index) order with exact fixed-point mass (:182-186) and the draw from the
+//      row's uniform, by one warp for up to 64 candidates (a block finish up to
+//      256, the general path over the whole row beyond).  A row whose candidate
+//      lists overflow is read again against the final bound.
 // Status: a NaN anywhere in the row, else a +inf tempered score, else no finite
 // score.  No inter-CTA communication and no scratch memory in global memory.
 #include <cuda_runtime.h>
+
+#include <type_traits>
 
 #include "sv_block.cuh"
 #include "sv_common.cuh"
@@ -37,96 +42,124 @@ namespace sv {
 
 namespace {
 
-// Resident CTAs per SM: 3 (256 threads, a 3-slot ring each) or 1 (512 threads, a
-// 12-slot ring).
-#ifndef SV_STREAM_CTAS_PER_SM
-#define SV_STREAM_CTAS_PER_SM 3
+constexpr int UB = 32;       // bytes per unit (one 256-bit load)
+constexpr int BU = 1;        // units per thread per batch
+constexpr int RING = 4;      // batches in registers (RING - 1 in flight while one is worked on)
+constexpr int QCAP = 32;     // queued hit units per warp
+constexpr int CAP = 1024;    // candidate capacity per row (split evenly between the warps)
+constexpr int SFIN = 256;    // candidates the fast finishes take
+constexpr int SBINS = 256;   // bound histogram bins
+constexpr int RW = 8;        // growth of a warp's list between its bound recomputations
+constexpr int IDV = 8;       // 16-byte history vectors per thread per load round
+#ifndef SV_STREAM_PREFETCH
+#define SV_STREAM_PREFETCH 8
 #endif
-constexpr int kCtasPerSm = SV_STREAM_CTAS_PER_SM;
-constexpr int SNT = kCtasPerSm == 1 ? 512 : 256;  // threads per CTA
-constexpr int SWARPS = SNT / 32;
-constexpr int SBUF = kCtasPerSm == 1 ? 12 : 3;  // ring slots
-constexpr size_t kSmemCap = kCtasPerSm == 1 ? 227 * 1024 : 74 * 1024;  // per CTA
-constexpr int SCHUNK = 16 * 1024;       // bytes per slot / chunk
-constexpr int SCU = SCHUNK / 16;        // 16-byte units per chunk
-constexpr int UPT = SCU / SNT;          // units per thread per chunk
-constexpr int SBINS = 256;              // bound histogram bins
-constexpr int UCAP = 704;               // hit units per row (their 16 bytes are kept)
-constexpr int SFIN = 256;               // candidates the fast finish handles after pruning
-constexpr int kBoundWarp = SWARPS - 1;  // computes the histogram bound after each chunk
-constexpr int kIssuer = 32;             // issues the bulk copies (warp 1: warp 0 may be finishing a row)
-constexpr int NB = SNT - 32;            // threads of warps 1.. that build a row's seen bitmap
+constexpr int PF0 = SV_STREAM_PREFETCH;  // batches prefetched into L2 while the bitmap is built
 
+template <int NT>
 struct __align__(16) StreamShared {
-  unsigned long long mbar[SBUF];
-  BlockScratch<SNT> bs;
+  BlockScratch<NT> bs;
   __align__(16) unsigned int bins[SBINS];
-  float gsort[SWARPS][16];  // first chunk: each warp's group values, descending
-  float first_raw;          //              and their kk-th largest
-  float te_pub;           // bound published by the bound warp, read after the next barrier
-  unsigned int rmax_key;  // ordered key of the row's largest raw score
-  int unit_n;
+  float wsort[NT / 32][32];  // first bound: each warp's values, descending
+  int wcount[NT / 32];       // candidates each warp found
+  __align__(16) uint4 qdata[NT / 32][2 * QCAP];  // each warp's queued hit units (32 bytes each)
+  int qunit[NT / 32][QCAP];                      // and their unit numbers
+  float boot_kth;            // kk-th largest of the first bound's values
+  unsigned int tau_key;      // ordered key of the shared bound (atomicMax)
+  unsigned int rmax_key;     // ordered key of the row's largest raw score
   int err;
-  __align__(16) uint4 udata[UCAP];  // hit units' 16 bytes; after the prune: finish scratch
-  int uidx[UCAP];                   // hit units: (unit << 8) | seen bits
-  __align__(16) unsigned char work[16 * SFIN];  // finish arrays / general-path scratch
+  __align__(16) float cval[CAP];  // candidates: penalised score, index; warp w owns
+  int cidx[CAP];                  // entries [w * CAP / warps, (w + 1) * CAP / warps)
+  __align__(16) float fv[SFIN];   // finish input: tempered score, index
+  int fi[SFIN];
 };
 
-constexpr size_t kStaticBytes = (sizeof(StreamShared) + 127) & ~size_t(127);
+__host__ __device__ constexpr size_t static_bytes(int nt) {
+  return nt == 128 ? (sizeof(StreamShared<128>) + 127) & ~size_t(127)
+         : nt == 256 ? (sizeof(StreamShared<256>) + 127) & ~size_t(127)
+                     : (sizeof(StreamShared<512>) + 127) & ~size_t(127);
+}
 
 __host__ __device__ inline size_t bitmap_bytes(int64_t V) {
   return (((size_t)V + 31) / 32 * 4 + 16 + 127) & ~size_t(127);
 }
 
-// Warps 1.. only (the row-start bitmap build, while warp 0 may still finish the
-// previous row).
-__device__ __forceinline__ void bar_builders() { asm volatile("bar.sync 1, %0;" ::"n"(NB) : "memory"); }
-
-// Geometry of one row's window: 16-byte units from the row start rounded down.
-struct RowGeom {
-  const unsigned char* base16;  // first unit
-  uintptr_t b_lo, b_hi;         // 16-byte-aligned interior [b_lo, b_hi)
-  int off_e;                    // window position of element 0
-  int nunits;
-  int nch;                      // chunks
+// A 32-byte unit in registers: 8 fp32 or 16 fp16/bf16 values.
+template <typename TIn> struct Unit;
+template <> struct Unit<float> {
+  static constexpr int E = 8;
+  __device__ static float at(const uint32_t (&w)[8], int e) { return __uint_as_float(w[e]); }
+  __device__ static void put(uint32_t (&w)[8], int e, float v) { w[e] = __float_as_uint(v); }
+};
+__device__ __forceinline__ void put16(uint32_t (&w)[8], int e, uint32_t b) {
+  w[e >> 1] = (e & 1) ? ((w[e >> 1] & 0xffffu) | (b << 16)) : ((w[e >> 1] & 0xffff0000u) | b);
+}
+template <> struct Unit<__half> {
+  static constexpr int E = 16;
+  __device__ static float at(const uint32_t (&w)[8], int e) {
+    float f;
+    const unsigned short h = (unsigned short)(w[e >> 1] >> (16 * (e & 1)));
+    asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+    return f;
+  }
+  __device__ static void put(uint32_t (&w)[8], int e, __half v) { put16(w, e, __half_as_ushort(v)); }
+};
+template <> struct Unit<__nv_bfloat16> {
+  static constexpr int E = 16;
+  __device__ static float at(const uint32_t (&w)[8], int e) {
+    return __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
+  }
+  __device__ static void put(uint32_t (&w)[8], int e, __nv_bfloat16 v) { put16(w, e, __bfloat16_as_ushort(v)); }
 };
 
-template <typename TIn>
-__device__ __forceinline__ RowGeom row_geom(const RowArgs& a, int64_t row) {
-  constexpr int ES = Elem<TIn>::kSize;
-  const TIn* rowp = reinterpret_cast<const TIn*>(a.logits) + row * a.row_stride;
-  const uintptr_t gs = reinterpret_cast<uintptr_t>(rowp);
-  const uintptr_t ge = gs + (uintptr_t)a.vocab * ES;
-  RowGeom g;
-  const uintptr_t b16 = gs & ~uintptr_t(15);
-  g.base16 = reinterpret_cast<const unsigned char*>(b16);
-  g.off_e = (int)((gs - b16) / ES);
-  g.nunits = (int)((ge - b16 + 15) / 16);
-  g.nch = (g.nunits + SCU - 1) / SCU;
-  g.b_lo = (gs + 15) & ~uintptr_t(15);
-  g.b_hi = ge & ~uintptr_t(15);
-  return g;
+__device__ __forceinline__ void load_unit(const unsigned char* p, uint32_t (&w)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+               : "l"(p));
 }
 
-// Issue chunk c of the row described by g into `slot` (one thread).
-__device__ __forceinline__ void issue_chunk(const RowGeom& g, int c, unsigned char* slot, void* bar) {
-  const uintptr_t w0 = reinterpret_cast<uintptr_t>(g.base16) + (uintptr_t)c * SCHUNK;
-  const uintptr_t w1 = reinterpret_cast<uintptr_t>(g.base16) + (uintptr_t)g.nunits * 16;
-  const uintptr_t lo = w0 > g.b_lo ? w0 : g.b_lo;
-  uintptr_t hi = w0 + SCHUNK < w1 ? w0 + SCHUNK : w1;
-  if (hi > g.b_hi) hi = g.b_hi;
-  if (hi > lo) {
-    const uint32_t bytes = (uint32_t)(hi - lo);
-    mbar_expect_tx(bar, bytes);
-    bulk_g2s(slot + (lo - w0), reinterpret_cast<const void*>(lo), bytes, bar);
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// NaN-propagating maximum of a unit (16-bit values: a packed-pair tree, two
+// conversions at the end).
+template <typename TIn>
+__device__ __forceinline__ float unit_max(const uint32_t (&w)[8]) {
+  using U = Unit<TIn>;
+  if constexpr (U::E == 8) {
+    const float a = max3_nan(U::at(w, 0), U::at(w, 1), U::at(w, 2));
+    const float b = max3_nan(U::at(w, 3), U::at(w, 4), U::at(w, 5));
+    return max3_nan(a, b, max_nan(U::at(w, 6), U::at(w, 7)));
   } else {
-    mbar_arrive(bar);
+    auto mx2 = [](uint32_t x, uint32_t y) {
+      uint32_t r;
+      if constexpr (sizeof(TIn) == 2 && std::is_same<TIn, __half>::value)
+        asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(y));
+      else
+        asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(y));
+      return r;
+    };
+    const uint32_t p = mx2(mx2(mx2(w[0], w[1]), mx2(w[2], w[3])), mx2(mx2(w[4], w[5]), mx2(w[6], w[7])));
+    const uint32_t q[8] = {p, 0, 0, 0, 0, 0, 0, 0};
+    return max_nan(U::at(q, 0), U::at(q, 1));
   }
+}
+
+// L2 prefetch of bytes [lo, hi) of global memory, trimmed to 16-byte bounds.
+__device__ __forceinline__ void prefetch_l2(uintptr_t lo, uintptr_t hi) {
+  lo = (lo + 15) & ~uintptr_t(15);
+  hi &= ~uintptr_t(15);
+  if (hi <= lo) return;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)(hi - lo)) : "memory");
 }
 
 // Seen bits of elements e0 .. e0+E-1 (indices outside [0, V) give 0).
 __device__ __forceinline__ uint32_t unit_bits(const uint32_t* bm, int64_t e0, int E, int64_t V) {
-  if (e0 >= 0 && (int)(e0 & 31) + E <= 32) return (bm[e0 >> 5] >> (e0 & 31)) & ((1u << E) - 1u);
+  if (e0 >= 0 && (int)(e0 & 31) + E <= 32 && e0 + E <= V)
+    return (bm[e0 >> 5] >> (e0 & 31)) & (E == 32 ? ~0u : ((1u << E) - 1u));
   uint32_t r = 0;
   for (int e = 0; e < E; ++e) {
     const int64_t i = e0 + e;
@@ -135,15 +168,20 @@ __device__ __forceinline__ uint32_t unit_bits(const uint32_t* bm, int64_t e0, in
   return r;
 }
 
-// The bound from the histogram (one warp): the highest bin b with at least kk group
-// maxima in bins >= b gives key base + (b << shift).  Returns the lowered bound in
-// the penalised domain, or -inf.  Lane l reads bins 8l .. 8l+7.
+// The bound from the histogram (one warp): the highest bin b with at least kk
+// counted values in bins >= b gives key base + (b << shift).  Returns the lowered
+// bound in the penalised domain, or -inf.  Lane l reads bins 8l .. 8l+7.
 __device__ __forceinline__ float hist_bound(const unsigned int* bins, uint32_t base_key, int shift, int kk,
                                             float T) {
   const int lane = threadIdx.x & 31;
-  const uint4 b0 = reinterpret_cast<const uint4*>(bins)[2 * lane];
-  const uint4 b1 = reinterpret_cast<const uint4*>(bins)[2 * lane + 1];
-  const uint32_t c[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  // Volatile loads: other warps are still counting.
+  uint32_t c[8];
+  asm volatile("ld.volatile.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+               : "r"(smem_u32(bins + 8 * lane)));
+  asm volatile("ld.volatile.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(c[4]), "=r"(c[5]), "=r"(c[6]), "=r"(c[7])
+               : "r"(smem_u32(bins + 8 * lane + 4)));
   uint32_t s = 0;
 #pragma unroll
   for (int q = 0; q < 8; ++q) s += c[q];
@@ -160,538 +198,612 @@ __device__ __forceinline__ float hist_bound(const unsigned int* bins, uint32_t b
     above += c[q];
     if (best < 0 && above >= (uint32_t)kk) best = lane * 8 + q;
   }
-  // The highest lane with a qualifying bin holds the answer.
   const unsigned m = __ballot_sync(0xffffffffu, best >= 0);
   if (!m) return Elem<float>::neg_inf();
   best = __shfl_sync(0xffffffffu, best, 31 - __clz(m));
   return lower_tau(key_to_float(base_key + ((uint32_t)best << shift)), T);
 }
 
-// Marks history ids staged in shared memory (16-byte vectors of Id) in the bitmap
-// (threads 32..); returns the ST_HISTORY error bit for ids outside [0, V).
-template <typename Id>
-__device__ __forceinline__ int mark_staged(const unsigned char* src, int64_t L, int64_t V, uint32_t* bits) {
-  constexpr int PER = 16 / (int)sizeof(Id);
-  int err = 0;
-  for (int64_t q = threadIdx.x - 32; q * PER < L; q += NB) {
-    Id id[PER];
-    *reinterpret_cast<uint4*>(id) = reinterpret_cast<const uint4*>(src)[q];
+// One unit of a row by element loads, -inf outside the row: the partial units at
+// a row's ends (out of line, so the batch loop keeps only the plain load).
+struct UnitVals {
+  uint4 a, b;
+};
+
+template <typename TIn>
+__device__ __noinline__ UnitVals guarded_unit(const TIn* rowp, int u, int off_e, int nunits, int64_t V) {
+  using U = Unit<TIn>;
+  uint32_t w[8];
 #pragma unroll
-    for (int t = 0; t < PER; ++t) {
-      if (q * PER + t >= L) break;
-      const int64_t x = (int64_t)id[t];
-      if (x < 0 || x >= V) {
-        err |= 1 << ST_HISTORY;
-      } else {
-        const uint32_t b = 1u << (x & 31);
-        uint32_t* w = &bits[x >> 5];
-        if (!(*w & b)) atomicOr(w, b);  // repeated ids mostly find their bit set
+  for (int e = 0; e < U::E; ++e) {
+    const int64_t i = (int64_t)u * U::E + e - off_e;
+    U::put(w, e, (u < nunits && i >= 0 && i < V) ? rowp[i] : Elem<TIn>::neg_inf());
+  }
+  UnitVals r;
+  r.a = make_uint4(w[0], w[1], w[2], w[3]);
+  r.b = make_uint4(w[4], w[5], w[6], w[7]);
+  return r;
+}
+
+// What a warp's queue drain needs besides the shared layout.
+struct DrainCtx {
+  float tau0, rp, T;
+  int off_e, kk, bin_shift;
+  uint32_t base_key;
+};
+
+template <int NT>
+__device__ __forceinline__ float shared_tau(const StreamShared<NT>& sh, float tau0) {
+  const float t = key_to_float(*reinterpret_cast<const volatile unsigned int*>(&sh.tau_key));
+  return fmaxf(fmaxf(tau0, t), -3.402823466e38f);  // excludes -inf
+}
+
+// Drains the calling warp's queue of qn hit units, one unit per lane: each element
+// whose penalised score reaches the current bound is appended to the warp's
+// candidate list (count cnt, ballot-aggregated) and counted in the histogram; a
+// list grown by RW entries since `last` recomputes the bound.  Returns {cnt, last}.
+template <typename TIn, int NT>
+__device__ __noinline__ int2 drain_queue(StreamShared<NT>* shp, const uint32_t* bits, int qn, int cnt, int last,
+                                         DrainCtx c) {
+  using U = Unit<TIn>;
+  constexpr int E = U::E;
+  constexpr int CAPW = CAP / (NT / 32);
+  constexpr unsigned FULL = 0xffffffffu;
+  StreamShared<NT>& sh = *shp;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  float* wval = sh.cval + warp * CAPW;
+  int* widx = sh.cidx + warp * CAPW;
+  __syncwarp();  // the queue's stores are visible to the warp
+  const float tc = shared_tau(sh, c.tau0);
+  const bool have = lane < qn;
+  uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int u = 0;
+  if (have) {
+    const uint4 p = sh.qdata[warp][2 * lane], q = sh.qdata[warp][2 * lane + 1];
+    w[0] = p.x; w[1] = p.y; w[2] = p.z; w[3] = p.w;
+    w[4] = q.x; w[5] = q.y; w[6] = q.z; w[7] = q.w;
+    u = sh.qunit[warp][lane];
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    float x = U::at(w, e);
+    bool pass = have && x >= tc;
+    if (!__any_sync(FULL, pass)) continue;
+    const int i = u * E + e - c.off_e;  // inside the row when pass: outside elements are -inf
+    if (pass && ((bits[i >> 5] >> (i & 31)) & 1u)) {
+      x = penalize(x, c.rp);
+      pass = x >= tc;
+    }
+    const unsigned bal = __ballot_sync(FULL, pass);
+    if (pass) {
+      const int pos = cnt + __popc(bal & lt_mask);
+      if (pos < CAPW) {
+        wval[pos] = x;
+        widx[pos] = i;
       }
+      const uint32_t k = ord_key(x);
+      if (k >= c.base_key)
+        atomicAdd(&sh.bins[min((uint32_t)(SBINS - 1), (k - c.base_key) >> c.bin_shift)], 1u);
+    }
+    cnt += __popc(bal);
+  }
+  __syncwarp();  // the queue may be refilled
+  if (cnt >= last + RW) {
+    last = cnt;
+    const float tb = hist_bound(sh.bins, c.base_key, c.bin_shift, c.kk, c.T);
+    if (lane == 0 && tb > Elem<float>::neg_inf()) atomicMax(&sh.tau_key, ord_key(tb));
+  }
+  return make_int2(cnt, last);
+}
+
+// The row's history ids in 16-byte vectors, IDV per thread per load round.
+struct IdRound {
+  uint4 v[IDV];
+};
+
+// Marks vectors [q0, q0 + IDV * NT) of a row's ids (held in r) in the shared
+// bitmap; returns the ST_HISTORY error bit for ids outside [0, V).
+template <int NT>
+__device__ __forceinline__ int mark_round(const IdRound& r, int64_t q0, int64_t nv, int64_t L, int idb, int64_t V,
+                                          uint32_t* bits) {
+  int err = 0;
+  auto mark = [&](int64_t x) {
+    if ((uint64_t)x >= (uint64_t)V) {
+      err |= 1 << ST_HISTORY;
+    } else {
+      const uint32_t b = 1u << (x & 31);
+      uint32_t* w = &bits[x >> 5];
+      if (!(*w & b)) atomicOr(w, b);  // repeated ids mostly find their bit set
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < IDV; ++k) {
+    const int64_t q = q0 + threadIdx.x + (int64_t)k * NT;
+    if (q >= nv) break;
+    const uint4 t = r.v[k];
+    if (idb == 4) {
+      const int32_t id[4] = {(int32_t)t.x, (int32_t)t.y, (int32_t)t.z, (int32_t)t.w};
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        if (q * 4 + s < L) mark(id[s]);
+    } else {
+      mark((int64_t)(((uint64_t)t.y << 32) | t.x));
+      if (q * 2 + 1 < L) mark((int64_t)(((uint64_t)t.w << 32) | t.z));
     }
   }
   return err;
 }
 
-template <typename TIn>
-__global__ void __launch_bounds__(SNT, kCtasPerSm) stream_kernel(const RowArgs a) {
+template <int NT>
+__device__ __forceinline__ void load_round(IdRound& r, const uint4* h, int64_t q0, int64_t nv) {
+#pragma unroll
+  for (int k = 0; k < IDV; ++k) {
+    const int64_t q = q0 + threadIdx.x + (int64_t)k * NT;
+    if (q < nv) r.v[k] = __ldg(h + q);
+  }
+}
+
+// The other history forms (unaligned ids, the packed bitmap, the bool mask).
+template <int NT>
+__device__ __forceinline__ int mark_other(const RowArgs& a, int64_t row, int64_t V, uint32_t* bits) {
+  const int tid = threadIdx.x;
+  const int nw = (int)((V + 31) >> 5);
+  int err = 0;
+  if (a.hist_kind == HIST_IDS32 || a.hist_kind == HIST_IDS64) {
+    const int64_t L = hist_length(a, row);
+    for (int64_t j = tid; j < L; j += NT) {
+      const int64_t x = hist_id(a, row, j);
+      if ((uint64_t)x >= (uint64_t)V) {
+        err |= 1 << ST_HISTORY;
+      } else {
+        const uint32_t b = 1u << (x & 31);
+        if (!(bits[x >> 5] & b)) atomicOr(&bits[x >> 5], b);
+      }
+    }
+  } else if (a.hist_kind == HIST_BITS32) {
+    const uint32_t* hb = reinterpret_cast<const uint32_t*>(a.hist) + row * a.hist_stride;
+    for (int w = tid; w < nw; w += NT) {
+      uint32_t v = hb[w];
+      if (w == nw - 1 && (V & 31)) v &= (1u << (V & 31)) - 1u;
+      bits[w] = v;
+    }
+  } else if (a.hist_kind == HIST_MASK8) {
+    for (int64_t i = tid; i < V; i += NT)
+      if (seen_global(a, row, i)) atomicOr(&bits[i >> 5], 1u << (i & 31));
+  }
+  return err;
+}
+
+// Resident CTAs per SM the register budget is sized for: 7 x 128 threads (1036
+// rows at once on 148 SMs), 3 x 256, 2 x 512.
+template <int NT>
+constexpr int min_blocks() {
+  return NT == 128 ? 7 : NT == 256 ? 3 : 2;
+}
+
+template <typename TIn, int NT>
+__global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  StreamShared& sh = *reinterpret_cast<StreamShared*>(smem_raw);
-  BlockScratch<SNT>& bs = sh.bs;
-  unsigned char* ring = smem_raw + kStaticBytes;
-  uint32_t* bits = reinterpret_cast<uint32_t*>(ring + (size_t)SBUF * SCHUNK);
+  using Sh = StreamShared<NT>;
+  Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
+  BlockScratch<NT>& bs = sh.bs;
+  uint32_t* bits = reinterpret_cast<uint32_t*>(smem_raw + static_bytes(NT));
+  using U = Unit<TIn>;
+  constexpr int E = U::E;
   constexpr int ES = Elem<TIn>::kSize;
-  constexpr int EPU = 16 / ES;
-  using IO = UnitIO<TIn>;
+  constexpr int NWARPS = NT / 32;
+  constexpr int CAPW = CAP / NWARPS;  // candidates per warp list
+  constexpr int BATCH = NT * BU;      // units per CTA batch
+  constexpr unsigned FULL = 0xffffffffu;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float NEG = Elem<float>::neg_inf();
   const float PINF = __int_as_float(0x7f800000);
   const int64_t V = a.vocab;
   const int nw = (int)((V + 31) >> 5);
   const float rp = a.rep_penalty, T = a.temperature;
-  const float rinv_lo = __frcp_rd(rp);  // <= 1/rp: x * rinv_lo rounded down <= x / rp rounded
   const int kk = a.kk;
-  const int64_t first = blockIdx.x, step = gridDim.x;
-  if (first >= a.rows) return;
+  const int64_t row = blockIdx.x;
+  const unsigned lt_mask = (1u << lane) - 1u;
 
-  // History ids travel through the ring ahead of their row when they fit a slot.
+  // Row geometry: 32-byte units from the row start rounded down.
+  const TIn* rowp = reinterpret_cast<const TIn*>(a.logits) + row * a.row_stride;
+  const uintptr_t gs = reinterpret_cast<uintptr_t>(rowp);
+  const uintptr_t ge = gs + (uintptr_t)V * ES;
+  const uintptr_t b32 = gs & ~uintptr_t(UB - 1);
+  const unsigned char* base = reinterpret_cast<const unsigned char*>(b32);
+  const int off_e = (int)((gs - b32) / ES);
+  const int nunits = (int)((ge - b32 + UB - 1) / UB);
+  const int u_lo = gs == b32 ? 0 : 1;          // first unit inside the row
+  const int u_hi = (int)((ge - b32) / UB);     // units [u_lo, u_hi) lie inside
+  const int nb = (nunits + BATCH - 1) / BATCH;
+
+  // Loads of batch b: whole batches inside the row take the 256-bit load; the
+  // partial ones at the row's ends go through guarded_unit.
+  const int bf0 = u_lo, bf1 = u_hi / BATCH;  // batches [bf0, bf1) lie inside the row
+  auto load_batch = [&](uint32_t (&w)[BU][8], int b) {
+    const int u = b * BATCH + tid;
+    if ((b >= bf0 && b < bf1) || (u >= u_lo && u < u_hi)) {
+      load_unit(base + (size_t)u * UB, w[0]);
+    } else {
+      const UnitVals r = guarded_unit<TIn>(rowp, u, off_e, nunits, V);
+      w[0][0] = r.a.x; w[0][1] = r.a.y; w[0][2] = r.a.z; w[0][3] = r.a.w;
+      w[0][4] = r.b.x; w[0][5] = r.b.y; w[0][6] = r.b.z; w[0][7] = r.b.w;
+    }
+  };
+
+  // 0. the first batches on their way into L2; the history ids in flight.
+  if (tid == 0) {
+    const uintptr_t hi = b32 + (uintptr_t)PF0 * BATCH * UB;
+    prefetch_l2(gs, hi < ge ? hi : ge);
+  }
   const bool ids_kind = a.hist_kind == HIST_IDS32 || a.hist_kind == HIST_IDS64;
   const int idb = a.hist_kind == HIST_IDS64 ? 8 : 4;
-  const size_t hbytes = ids_kind ? (size_t)a.hist_cols * idb : 0;
-  const bool stage_ids = ids_kind && hbytes > 0 && hbytes <= SCHUNK && hbytes % 16 == 0 &&
-                         (reinterpret_cast<uintptr_t>(a.hist) % 16) == 0 && ((size_t)a.hist_stride * idb) % 16 == 0;
+  const int64_t L = ids_kind ? hist_length(a, row) : 0;
+  const uint4* h4 = ids_kind ? reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(a.hist) +
+                                                              (size_t)row * a.hist_stride * idb)
+                             : nullptr;
+  const bool vec_ids = ids_kind && (reinterpret_cast<uintptr_t>(h4) & 15) == 0;
+  const int64_t nv = vec_ids ? (L * idb + 15) / 16 : 0;
+  IdRound idr;
+  if (vec_ids) load_round<NT>(idr, h4, 0, nv);
 
-  // Issue cursor (thread 0 only): ic = -1 is the row's ids, then its chunks.
-  int64_t irow = first;
-  int ic = stage_ids ? -1 : 0;
-  RowGeom ig = row_geom<TIn>(a, irow);
-  int islot = 0;  // ring slot of the next issue
-  if (tid == 0) {
-    for (int s = 0; s < SBUF; ++s) mbar_init(&sh.mbar[s], 1);
-    mbar_init_fence();
-    sh.err = 0;
+  // 1. seen bitmap.
+  {
+    const int nz = (nw + 4 + 3) >> 2;  // 16-byte words, within bitmap_bytes(V)
+    for (int q = tid; q < nz; q += NT) reinterpret_cast<uint4*>(bits)[q] = make_uint4(0, 0, 0, 0);
+    for (int q = tid; q < SBINS / 4; q += NT) reinterpret_cast<uint4*>(sh.bins)[q] = make_uint4(0, 0, 0, 0);
+    if (tid == 0) {
+      sh.err = 0;
+      sh.rmax_key = 0;
+      sh.tau_key = ord_key(NEG);
+      sh.boot_kth = NEG;
+    }
   }
   __syncthreads();
-  auto issue_next = [&]() {  // thread kIssuer, after a barrier
-    if (irow >= a.rows) return;
-    fence_proxy_async_smem();
-    const int s = islot;
-    unsigned char* slot = ring + (size_t)s * SCHUNK;
-    if (ic < 0) {
-      mbar_expect_tx(&sh.mbar[s], (uint32_t)hbytes);
-      bulk_g2s(slot, reinterpret_cast<const unsigned char*>(a.hist) + (size_t)irow * a.hist_stride * idb,
-               (uint32_t)hbytes, &sh.mbar[s]);
+  {
+    int e = 0;
+    if (vec_ids) {
+      e = mark_round<NT>(idr, 0, nv, L, idb, V, bits);
+      for (int64_t q0 = (int64_t)IDV * NT; q0 < nv; q0 += (int64_t)IDV * NT) {
+        load_round<NT>(idr, h4, q0, nv);
+        e |= mark_round<NT>(idr, q0, nv, L, idb, V, bits);
+      }
     } else {
-      issue_chunk(ig, ic, slot, &sh.mbar[s]);
+      e = mark_other<NT>(a, row, V, bits);
     }
-    if (++islot == SBUF) islot = 0;
-    if (++ic == ig.nch) {
-      ic = stage_ids ? -1 : 0;
-      irow += step;
-      if (irow < a.rows) ig = row_geom<TIn>(a, irow);
-    }
-  };
-  if (tid == kIssuer)
-    for (int s = 0; s < SBUF; ++s) issue_next();
+    if (e) atomicOr(&sh.err, e);
+  }
+  __syncthreads();
 
-  // Ring slot and mbarrier phase of the next slot to consume (all threads).
-  int cslot = 0;
-  uint32_t cphase = 0;
-  auto consume_next = [&]() {
-    if (++cslot == SBUF) {
-      cslot = 0;
-      cphase ^= 1u;
-    }
-  };
-
-  for (int64_t row = first; row < a.rows; row += step) {
-    const RowGeom g = row_geom<TIn>(a, row);
-    const TIn* rowp = reinterpret_cast<const TIn*>(a.logits) + row * a.row_stride;
-    const bool aligned = g.off_e == 0;
-    // 1. seen bitmap of the row, by warps 1.. (warp 0 may still be finishing the
-    //    previous row; it joins at the barrier before the chunks).
-    if (warp > 0) {
-      const int bt = tid - 32;
-      {
-        const int nz = (nw + 4 + 3) >> 2;  // 16-byte words, within bitmap_bytes(V)
-        for (int w = bt; w < nz; w += NB) reinterpret_cast<uint4*>(bits)[w] = make_uint4(0, 0, 0, 0);
-      }
-      if (bt < SBINS / 4) reinterpret_cast<uint4*>(sh.bins)[bt] = make_uint4(0, 0, 0, 0);
-      if (tid == kIssuer) {
-        sh.unit_n = 0;
-        sh.te_pub = NEG;
-        sh.rmax_key = 0;
-        sh.err = 0;
-      }
-      bar_builders();
-      int local_err = 0;
-      if (ids_kind) {
-        const int64_t L = hist_length(a, row);
-        if (stage_ids) {
-          if (!mbar_wait(&sh.mbar[cslot], cphase)) local_err |= 1 << ST_TIMEOUT;
-          const unsigned char* src = ring + (size_t)cslot * SCHUNK;
-          local_err |= idb == 4 ? mark_staged<int32_t>(src, L, V, bits) : mark_staged<int64_t>(src, L, V, bits);
-          bar_builders();  // the ids slot is consumed
-          if (tid == kIssuer) issue_next();
-        } else {
-          for (int64_t j = bt; j < L; j += NB) {
-            const int64_t x = hist_id(a, row, j);
-            if (x < 0 || x >= V) {
-              local_err |= 1 << ST_HISTORY;
-            } else {
-              const uint32_t b = 1u << (x & 31);
-              if (!(bits[x >> 5] & b)) atomicOr(&bits[x >> 5], b);
-            }
-          }
-        }
-      } else if (a.hist_kind == HIST_BITS32) {
-        const uint32_t* hb = reinterpret_cast<const uint32_t*>(a.hist) + row * a.hist_stride;
-        for (int w = bt; w < nw; w += NB) {
-          uint32_t v = hb[w];
-          if (w == nw - 1 && (V & 31)) v &= (1u << (V & 31)) - 1u;
-          bits[w] = v;
-        }
-      } else if (a.hist_kind == HIST_MASK8) {
-        for (int64_t i = bt; i < V; i += NB)
-          if (seen_global(a, row, i)) atomicOr(&bits[i >> 5], 1u << (i & 31));
-      }
-      if (local_err) atomicOr(&sh.err, local_err);
-    }
-    if (stage_ids) consume_next();  // every thread keeps the ring position
-    __syncthreads();
-
-    // 2. chunks.
-    float te = NEG;         // current bound (penalised domain)
-    float rmx = NEG;        // NaN-propagating maximum of this thread's raw scores
-    uint32_t base_key = 0;  // histogram origin and bin width (identical in all threads)
-    int bin_shift = 0;
-    for (int c = 0; c < g.nch; ++c, consume_next()) {
-      TIn* slot = reinterpret_cast<TIn*>(ring + (size_t)cslot * SCHUNK);
-      if (!mbar_wait(&sh.mbar[cslot], cphase)) atomicOr(&sh.err, 1 << ST_TIMEOUT);
-      const int u0 = c * SCU;
-      const int un = min(SCU, g.nunits - u0);
-      // Ragged units (outside the aligned interior) come from global memory, with
-      // -inf outside the row; each unit belongs to one thread.
-      if (!aligned || un < SCU || g.b_hi < reinterpret_cast<uintptr_t>(g.base16) + (uintptr_t)g.nunits * 16) {
-        for (int k = tid; k < un; k += SNT) {
-          const uintptr_t ua = reinterpret_cast<uintptr_t>(g.base16) + (uintptr_t)(u0 + k) * 16;
-          if (ua < g.b_lo || ua >= g.b_hi) {
-#pragma unroll
-            for (int e = 0; e < EPU; ++e) {
-              const int64_t ei = (int64_t)(u0 + k) * EPU + e - g.off_e;
-              slot[k * EPU + e] = (ei >= 0 && ei < V) ? __ldg(rowp + ei) : Elem<TIn>::neg_inf();
-            }
-          }
-        }
-      }
-      // Unit maxima, seen bits and this lane's group value.  A unit with a seen
-      // token enters the group value through a lower bound of its penalised
-      // maximum.  Full chunks
-      // of aligned rows (the common case) take a path without bounds checks, their
-      // units at a fixed bit offset in consecutive bitmap words.
-      float umax[UPT];
-      uint32_t sb[UPT];
-      float gsrc = NEG;
-      auto unit = [&](int j, const float (&v)[EPU], float m, uint32_t bitsj) {
-        // At or below the unit's penalised maximum (the penalty is monotone and
-        // never raises a score; its lower bounds are products rounded down, no
-        // division): for a unit with a seen token, the penalty bound of its raw
-        // maximum, or, when that maximum reaches the bound (only such values can
-        // enter the histogram), the larger of its unseen elements' maximum and the
-        // penalty bound of its largest seen element.
-        float gv = m;
-        if (bitsj) {
-          gv = __fmul_rd(m, m < 0.0f ? rp : rinv_lo);
-          if (m >= te) {
-            float mu = NEG, ms = NEG;
-#pragma unroll
-            for (int e = 0; e < EPU; ++e) {
-              if ((bitsj >> e) & 1u) ms = fmaxf(ms, v[e]);
-              else mu = fmaxf(mu, v[e]);
-            }
-            gv = fmaxf(mu, __fmul_rd(ms, ms < 0.0f ? rp : rinv_lo));
-          }
-        }
-        umax[j] = m;
-        sb[j] = bitsj;
-        rmx = max_nan(rmx, m);
-        gsrc = fmaxf(gsrc, gv);  // fmaxf drops NaN; rmx reports it
-      };
-      if (aligned && un == SCU) {
-        const int e0 = (u0 + tid) * EPU;
-        const uint32_t* bw = bits + (e0 >> 5);
-        const int shf = e0 & 31;
-#pragma unroll
-        for (int j = 0; j < UPT; ++j) {
-          float v[EPU];
-          IO::load(slot, tid + j * SNT, v);
-          float m = v[0];
-#pragma unroll
-          for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
-          unit(j, v, m, (bw[j * (SNT * EPU / 32)] >> shf) & ((1u << EPU) - 1u));
-        }
+  // 2. the first RING batches (one unit per thread each); the first bound: the
+  //    kk-th largest of the threads' maxima over their unseen elements (in the
+  //    order value desc, warp, lane).
+  uint32_t w0[1][8], w1[1][8], w2[1][8], w3[1][8];
+  load_batch(w0, 0);
+  load_batch(w1, 1);
+  load_batch(w2, 2);
+  load_batch(w3, 3);
+  float boot;
+  {
+    float g = NEG;
+    auto boot_unit = [&](const uint32_t (&w)[1][8], int u) {
+      const int64_t e0 = (int64_t)u * E - off_e;
+      const uint32_t sb = off_e == 0 && u < u_hi ? (bits[e0 >> 5] >> (e0 & 31)) & ((1u << E) - 1u)
+                                                 : unit_bits(bits, e0, E, V);
+      if (!sb) {
+        g = max_nan(g, unit_max<TIn>(w[0]));
       } else {
 #pragma unroll
-        for (int j = 0; j < UPT; ++j) {
-          const int k = tid + j * SNT;
-          float m = NEG;
-          uint32_t b = 0;
-          float v[EPU];
-#pragma unroll
-          for (int e = 0; e < EPU; ++e) v[e] = NEG;
-          if (k < un) {
-            b = aligned ? (bits[((u0 + k) * EPU) >> 5] >> (((u0 + k) * EPU) & 31)) & ((1u << EPU) - 1u)
-                        : unit_bits(bits, (int64_t)(u0 + k) * EPU - g.off_e, EPU, V);
-            IO::load(slot, k, v);
-            m = v[0];
-#pragma unroll
-            for (int e = 1; e < EPU; ++e) m = max_nan(m, v[e]);
-          }
-          unit(j, v, m, b);
-        }
+        for (int e = 0; e < E; ++e)
+          if (!((sb >> e) & 1u)) g = fmaxf(g, U::at(w[0], e));
       }
-      const float gm = fmaxf(gsrc, __shfl_xor_sync(0xffffffffu, gsrc, 1));  // lane-pair group value
-      if (c == 0) {
-        // First bound: the exact kk-th largest of the chunk's 128 group values in
-        // the order (value desc, warp, group).  Each warp sorts its 16 by rank; a
-        // value's global rank adds its position in the other warps' lists (binary
-        // search); the value of rank kk - 1 is the bound.
-        const int pair = lane >> 1;
-        int rank = 0;
+    };
+    boot_unit(w0, tid);
+    boot_unit(w1, BATCH + tid);
+    boot_unit(w2, 2 * BATCH + tid);
+    boot_unit(w3, 3 * BATCH + tid);
+    if (g != g) g = NEG;  // NaN rows fail with ST_NAN; keep the ranks well defined
+    int rank = 0;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const float w = __shfl_sync(0xffffffffu, gm, 2 * q);
-          rank += (w > gm) || (w == gm && q < pair);
-        }
-        if ((lane & 1) == 0) sh.gsort[warp][rank] = gm;
-        __syncthreads();
-#pragma unroll
-        for (int w = 0; w < SWARPS; ++w) {
-          if (w == warp) continue;
-          int lo = 0, hi = 16;  // entries of warp w that come before this value
-#pragma unroll
-          for (int it = 0; it < 5; ++it) {
-            if (lo < hi) {
-              const int mid = (lo + hi) >> 1;
-              const float e = sh.gsort[w][mid];
-              if (e > gm || (e == gm && w < warp)) lo = mid + 1;
-              else hi = mid;
-            }
-          }
-          rank += lo;
-        }
-        if ((lane & 1) == 0 && rank == kk - 1) sh.first_raw = gm;
-        __syncthreads();
-        const float raw = sh.first_raw;
-        float hi = sh.gsort[0][0];
-#pragma unroll
-        for (int w = 1; w < SWARPS; ++w) hi = fmaxf(hi, sh.gsort[w][0]);
-        base_key = ord_key(raw);
-        const uint32_t span = ord_key(hi) > base_key ? ord_key(hi) - base_key : 0u;
-        bin_shift = 0;
-        while ((span >> bin_shift) >= (uint32_t)SBINS) ++bin_shift;
-        te = lower_tau(raw, T);
-      }
-      // Hit units: their maximum reaches the bound (the raw maximum bounds the
-      // penalised one from above).  Their 16 bytes and seen bits are kept for the
-      // finish, which tests their elements.
-      const float tcmp = fmaxf(te, -3.402823466e38f);  // excludes -inf
-      uint32_t hu = 0;
-#pragma unroll
-      for (int j = 0; j < UPT; ++j) hu |= (uint32_t)(umax[j] >= tcmp) << j;
-      if (hu) {
-        int pos = atomicAdd(&sh.unit_n, __popc(hu));
-#pragma unroll
-        for (int j = 0; j < UPT; ++j) {
-          if ((hu >> j) & 1u) {
-            if (pos < UCAP) {
-              const int k = tid + j * SNT;
-              sh.udata[pos] = reinterpret_cast<const uint4*>(slot)[k];
-              sh.uidx[pos] = ((u0 + k) << 8) | (int)sb[j];
-            }
-            ++pos;
-          }
-        }
-      }
-      // Histogram of the group values that can still raise the bound.
-      if ((lane & 1) == 0) {
-        const uint32_t k = ord_key(gm);
-        if (gm >= te && k >= base_key)
-          atomicAdd(&sh.bins[min((uint32_t)(SBINS - 1), (k - base_key) >> bin_shift)], 1u);
-      }
-      // The bound warp publishes a bound from the bins as they stand, before the
-      // barrier so that its latency overlaps the other warps' passes (counts only
-      // grow, so a partial histogram gives a valid, lower bound).  Every fourth
-      // chunk only: the scan sits on each chunk's critical path, and a bound a few
-      // chunks older keeps a few more units.
-      if (warp == kBoundWarp && (c & 3) == 3) {
-        __syncwarp();
-        const float tb = hist_bound(sh.bins, base_key, bin_shift, kk, T);
-        if (lane == 0) sh.te_pub = fmaxf(sh.te_pub, tb);
-      }
-      __syncthreads();  // the slot is consumed
-      te = fmaxf(te, sh.te_pub);
-      if (tid == kIssuer) issue_next();
+    for (int q = 0; q < 32; ++q) {
+      const float o = __shfl_sync(FULL, g, q);
+      rank += (o > g) || (o == g && q < lane);
     }
-    // The final bound, from the complete bins.
-    if (warp == kBoundWarp) {
-      const float tb = hist_bound(sh.bins, base_key, bin_shift, kk, T);
-      if (lane == 0) sh.te_pub = fmaxf(sh.te_pub, tb);
-    }
-
-    // 3. finish the row.
-    if (rmx != rmx) atomicOr(&sh.err, 1 << ST_NAN);
-    else if (rmx == PINF) atomicOr(&sh.err, 1 << ST_POSINF);
-    rmx = warp_max_nan(rmx);
-    if (lane == 0 && rmx == rmx) atomicMax(&sh.rmax_key, ord_key(rmx));
-    if (tid == 0) bs.flag = 0;
+    sh.wsort[warp][rank] = g;
     __syncthreads();
-    const float tfin = fmaxf(fmaxf(te, sh.te_pub), -3.402823466e38f);  // final bound; excludes -inf
-    const float uu = a.uniforms[row];
-    const int nu = sh.unit_n;
-    int status = sh.err ? first_err(sh.err) : ST_OK;
-    bool general = status == ST_OK && a.force_slow;
-    float* sval = reinterpret_cast<float*>(sh.work);
-    int* sidx = reinterpret_cast<int*>(sh.work + 4 * SFIN);
-    uint64_t* W = reinterpret_cast<uint64_t*>(sh.work + 8 * SFIN);
-    float* fv = reinterpret_cast<float*>(W);
-    int* fi = reinterpret_cast<int*>(sh.work + 12 * SFIN);
-    // Kept list and leader_fast's key array, in the unit data (consumed by then).
-    int* kidx = reinterpret_cast<int*>(sh.udata) + 2 * SFIN;
-    float* kval = reinterpret_cast<float*>(sh.udata);
-    int m = 0;
-    if (status == ST_OK && !general) {
-      // The elements of the hit units whose penalised score reaches the final
-      // bound, tempered (elements outside the row were staged as -inf).  When the
-      // list overflowed, the row is read again (from L2 or HBM) against that bound.
-      int bad = 0;
-      auto take = [&](int i, float x) {
-        const float tx = temper(x, T);
-        bad |= tx == PINF;
-        const int at = atomicAdd(&bs.flag, 1);
-        if (at < SFIN) {
-          fv[at] = tx;
-          fi[at] = i;
-        }
-      };
-      if (nu > UCAP) {
-        for (int64_t i = tid; i < V; i += SNT) {
-          float x = Elem<TIn>::load(rowp + i);
-          if (x >= tfin) {
-            if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
-            if (x >= tfin) take((int)i, x);
-          }
-        }
-      }
-      for (int t = tid; t < (nu > UCAP ? 0 : nu); t += SNT) {
-        const int ent = sh.uidx[t];
-        const int uid = ent >> 8;
-        float v[EPU];
-        IO::load(reinterpret_cast<const TIn*>(sh.udata), t, v);
 #pragma unroll
-        for (int e = 0; e < EPU; ++e) {
-          if (v[e] >= tfin) {
-            const int i = uid * EPU + e - g.off_e;
-            float x = v[e];
-            if ((ent >> e) & 1) x = penalize(x, rp);
-            if (x >= tfin) take(i, x);
-          }
+    for (int ow = 0; ow < NWARPS; ++ow) {
+      if (ow == warp) continue;
+      int lo = 0, hi = 32;  // entries of warp ow that come before this value
+#pragma unroll
+      for (int it = 0; it < 6; ++it) {
+        if (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          const float e = sh.wsort[ow][mid];
+          if (e > g || (e == g && ow < warp)) lo = mid + 1;
+          else hi = mid;
         }
       }
-      if (bad) atomicOr(&sh.err, 1 << ST_POSINF);
-      __syncthreads();
-      m = bs.flag;
-      if (sh.err) status = first_err(sh.err);
-      __syncthreads();
-      if (m > SFIN) general = status == ST_OK;
+      rank += lo;
     }
-    if (general && temper(key_to_float(sh.rmax_key), T) == PINF) {
-      // A score may reach +inf only through the temperature: check every element.
-      int inf = 0;
-      for (int64_t i = tid; i < V; i += SNT) {
+    if (rank == kk - 1) sh.boot_kth = g;
+    __syncthreads();
+    boot = sh.boot_kth;
+  }
+  float hi_boot = sh.wsort[0][0];
+#pragma unroll
+  for (int ow = 1; ow < NWARPS; ++ow) hi_boot = fmaxf(hi_boot, sh.wsort[ow][0]);
+  const uint32_t base_key = ord_key(boot);
+  int bin_shift = 0;
+  {
+    const uint32_t span = ord_key(hi_boot) > base_key ? ord_key(hi_boot) - base_key : 0u;
+    while ((span >> bin_shift) >= (uint32_t)SBINS) ++bin_shift;
+  }
+  const float tau0 = lower_tau(boot, T);
+
+  // 3. batches.  A unit whose maximum reaches the bound is queued (its 32 bytes
+  //    and unit number) in the warp's queue; a full queue is drained, one unit per
+  //    lane.  The bound is read from shared memory once per ring turn and after
+  //    each drain.
+  float rmx = NEG;  // NaN-propagating maximum of this thread's raw scores
+  int cnt = 0;      // this warp's candidates (warp-uniform)
+  int last = 0;     // cnt at the warp's last bound recomputation
+  int qn = 0;       // queued units (warp-uniform)
+  const DrainCtx dc = {tau0, rp, T, off_e, kk, bin_shift, base_key};
+  float tc = shared_tau(sh, tau0);
+  auto process = [&](const uint32_t (&w)[BU][8], int b) {
+    const float um = unit_max<TIn>(w[0]);
+    rmx = max_nan(rmx, um);
+    const bool hit = um >= tc;
+    const unsigned bal = __ballot_sync(FULL, hit);
+    if (bal) {
+      const int n = __popc(bal);
+      if (qn + n > QCAP) {
+        const int2 r = drain_queue<TIn, NT>(&sh, bits, qn, cnt, last, dc);
+        cnt = r.x;
+        last = r.y;
+        qn = 0;
+        tc = shared_tau(sh, tau0);
+      }
+      if (hit) {
+        const int pos = qn + __popc(bal & lt_mask);
+        sh.qdata[warp][2 * pos] = make_uint4(w[0][0], w[0][1], w[0][2], w[0][3]);
+        sh.qdata[warp][2 * pos + 1] = make_uint4(w[0][4], w[0][5], w[0][6], w[0][7]);
+        sh.qunit[warp][pos] = b * BATCH + tid;
+      }
+      qn += n;
+    }
+  };
+  for (int b = 0; b < nb; b += RING) {
+    process(w0, b);
+    if (b + RING < nb) load_batch(w0, b + RING);
+    if (b + 1 < nb) {
+      process(w1, b + 1);
+      if (b + 1 + RING < nb) load_batch(w1, b + 1 + RING);
+    }
+    if (b + 2 < nb) {
+      process(w2, b + 2);
+      if (b + 2 + RING < nb) load_batch(w2, b + 2 + RING);
+    }
+    if (b + 3 < nb) {
+      process(w3, b + 3);
+      if (b + 3 + RING < nb) load_batch(w3, b + 3 + RING);
+    }
+    tc = shared_tau(sh, tau0);
+  }
+  if (qn) {
+    const int2 r = drain_queue<TIn, NT>(&sh, bits, qn, cnt, last, dc);
+    cnt = r.x;
+  }
+
+  // 4. finish the row.
+  if (rmx != rmx) atomicOr(&sh.err, 1 << ST_NAN);
+  else if (rmx == PINF) atomicOr(&sh.err, 1 << ST_POSINF);
+  rmx = warp_max_nan(rmx);
+  if (lane == 0) {
+    if (rmx == rmx) atomicMax(&sh.rmax_key, ord_key(rmx));
+    sh.wcount[warp] = cnt;
+  }
+  if (tid == 0) bs.flag = 0;
+  __syncthreads();
+  // The final bound from the complete bins (every warp computes the same value).
+  const float tfin = fmaxf(shared_tau(sh, tau0), hist_bound(sh.bins, base_key, bin_shift, kk, T));
+  const float uu = a.uniforms[row];
+  bool overflow = false;
+#pragma unroll
+  for (int ow = 0; ow < NWARPS; ++ow) overflow |= sh.wcount[ow] > CAPW;
+  int status = sh.err ? first_err(sh.err) : ST_OK;
+  bool general = status == ST_OK && a.force_slow;
+  float* fv = sh.fv;
+  int* fi = sh.fi;
+  // Finish scratch in the candidate lists (consumed by then).
+  float* sval = sh.cval;
+  int* sidx = reinterpret_cast<int*>(sh.cval + SFIN);
+  uint64_t* Wb = reinterpret_cast<uint64_t*>(sh.cval + 2 * SFIN);
+  uint64_t* Pb = reinterpret_cast<uint64_t*>(sh.cidx);
+  int* kidx = reinterpret_cast<int*>(sh.cidx) + 2 * SFIN;
+  float* kval = reinterpret_cast<float*>(sh.cidx);
+  int m = 0;
+  if (status == ST_OK && !general) {
+    // The candidates whose penalised score reaches the final bound, tempered.
+    // When a list overflowed, the row is read again (from L2 or HBM).
+    int bad = 0;
+    auto take = [&](int i, float x) {
+      const float tx = temper(x, T);
+      bad |= tx == PINF;
+      const int at = atomicAdd(&bs.flag, 1);
+      if (at < SFIN) {
+        fv[at] = tx;
+        fi[at] = i;
+      }
+    };
+    if (overflow) {
+      for (int64_t i = tid; i < V; i += NT) {
         float x = Elem<TIn>::load(rowp + i);
-        if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
-        inf |= temper(x, T) == PINF;
-      }
-      if (__syncthreads_or(inf)) {
-        status = ST_POSINF;
-        general = false;
-      }
-    }
-    if (status == ST_OK && !general && m == 0) status = ST_ALLNEGINF;
-    if (status == ST_OK && !general && m <= 64 && !(a.out_dense && a.dense_mode != DENSE_NONE)) {
-      // Common case: warp 0 finishes the row in registers while the other warps
-      // start the next one (it touches nothing the next row's start uses).
-      if (warp == 0) {
-        int64_t tok = -1;
-        const Kept kp = warp_finish<2>(a, fv, fi, m, uu, &tok, kidx, kval);
-        const float Sf = fix_to_float(kp.tot);
-        for (int j = lane; j < kp.n && j < a.out_cap; j += 32) {
-          if (a.out_idx) a.out_idx[row * a.out_cap + j] = kidx[j];
-          if (a.out_prob) a.out_prob[row * a.out_cap + j] = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kp.M)), Sf);
-          if (a.out_score) a.out_score[row * a.out_cap + j] = kval[j];
-        }
-        if (lane == 0) {
-          a.out_token[row] = tok;
-          if (a.out_count) a.out_count[row] = kp.n;
-          if (a.out_status) a.out_status[row] = ST_OK;
-          if (a.seen_bits && tok >= 0) atomicOr(&a.seen_bits[row * a.seen_bits_stride + (tok >> 5)], 1u << (tok & 31));
+        if (x >= tfin) {
+          if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
+          if (x >= tfin) take((int)i, x);
         }
       }
-      continue;
-    }
-    Kept kept = {0, 0.0f, 0};
-    int64_t token = -1;
-    if (a.out_dense && a.dense_mode != DENSE_NONE && status == ST_OK && !general) {
-      const float dv = a.dense_mode == DENSE_SCORES ? NEG : 0.0f;
-      for (int64_t i = tid; i < V; i += SNT) a.out_dense[row * a.dense_stride + i] = dv;
-      __syncthreads();
-    }
-    if (status == ST_OK && !general) {
-      if (m <= 64) {
-        // Few candidates: one warp finishes in registers.
-        if (warp == 0) {
-          kept = warp_finish<2>(a, fv, fi, m, uu, &token, kidx, kval);
-          if (lane == 0) {
-            bs.flag2 = kept.n;
-            bs.fval = kept.M;
-            bs.u64a = kept.tot;
-          }
+    } else {
+      for (int q = tid; q < CAP; q += NT) {
+        if (q % CAPW < sh.wcount[q / CAPW]) {
+          const float x = sh.cval[q];
+          if (x >= tfin) take(sh.cidx[q], x);
         }
-        __syncthreads();
-        kept.n = bs.flag2;
-        kept.M = bs.fval;
-        kept.tot = bs.u64a;
-      } else {
-        kept = leader_fast<SNT>(a, bs, fv, fi, m, sval, sidx, W, reinterpret_cast<uint64_t*>(sh.udata), kidx, kval);
-        token = draw_kept<SNT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(sh.work));
       }
-      const float Sf = fix_to_float(kept.tot);
-      for (int j = tid; j < kept.n; j += SNT) {
-        const float p = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kept.M)), Sf);
-        if (j < a.out_cap) {
-          if (a.out_idx) a.out_idx[row * a.out_cap + j] = kidx[j];
-          if (a.out_prob) a.out_prob[row * a.out_cap + j] = p;
-          if (a.out_score) a.out_score[row * a.out_cap + j] = kval[j];
-        }
-        if (a.out_dense && a.dense_mode != DENSE_NONE)
-          a.out_dense[row * a.dense_stride + kidx[j]] = a.dense_mode == DENSE_SCORES ? kval[j] : p;
-      }
-    } else if (general) {
-      auto seen = [&](int64_t i) -> bool { return (bits[i >> 5] >> (i & 31)) & 1u; };
-      auto emit = [&](int pos, int idx, float val, float Sf, float M) {
-        if (pos < a.out_cap) {
-          if (a.out_idx) a.out_idx[row * a.out_cap + pos] = idx;
-          if (a.out_prob) a.out_prob[row * a.out_cap + pos] = __fdiv_rn(sv_exp(__fsub_rn(val, M)), Sf);
-          if (a.out_score) a.out_score[row * a.out_cap + pos] = val;
-        }
-      };
-      kept = leader_slow<SNT, TIn, MODE_SAMPLE>(a, bs, sh.work, row, 0.0f, 0.0f, uu, &token, seen, emit);
-    } else if (a.out_dense && a.dense_mode != DENSE_NONE) {
-      const float dv = a.dense_mode == DENSE_SCORES ? NEG : 0.0f;
-      for (int64_t i = tid; i < V; i += SNT) a.out_dense[row * a.dense_stride + i] = dv;
     }
-    if (tid == 0) {
-      a.out_token[row] = status == ST_OK ? token : -1;
-      if (a.out_count) a.out_count[row] = kept.n;
-      if (a.out_status) a.out_status[row] = status;
-      if (status == ST_OK && a.seen_bits && token >= 0)
-        atomicOr(&a.seen_bits[row * a.seen_bits_stride + (token >> 5)], 1u << (token & 31));
-    }
+    if (bad) atomicOr(&sh.err, 1 << ST_POSINF);
     __syncthreads();
+    m = bs.flag;
+    if (sh.err) status = first_err(sh.err);
+    __syncthreads();
+    if (m > SFIN) general = status == ST_OK;
+  }
+  if (general && temper(key_to_float(sh.rmax_key), T) == PINF) {
+    // A score may reach +inf only through the temperature: check every element.
+    int inf = 0;
+    for (int64_t i = tid; i < V; i += NT) {
+      float x = Elem<TIn>::load(rowp + i);
+      if ((bits[i >> 5] >> (i & 31)) & 1u) x = penalize(x, rp);
+      inf |= temper(x, T) == PINF;
+    }
+    if (__syncthreads_or(inf)) {
+      status = ST_POSINF;
+      general = false;
+    }
+  }
+  if (status == ST_OK && !general && m == 0) status = ST_ALLNEGINF;
+  const bool dense = a.out_dense && a.dense_mode != DENSE_NONE;
+  if (status == ST_OK && !general && m <= 64 && !dense) {
+    // Common case: warp 0 finishes the row in registers.
+    if (warp == 0) {
+      int64_t tok = -1;
+      const Kept kp = warp_finish<2>(a, fv, fi, m, uu, &tok, kidx, kval);
+      const float Sf = fix_to_float(kp.tot);
+      for (int j = lane; j < kp.n && j < a.out_cap; j += 32) {
+        if (a.out_idx) a.out_idx[row * a.out_cap + j] = kidx[j];
+        if (a.out_prob) a.out_prob[row * a.out_cap + j] = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kp.M)), Sf);
+        if (a.out_score) a.out_score[row * a.out_cap + j] = kval[j];
+      }
+      if (lane == 0) {
+        a.out_token[row] = tok;
+        if (a.out_count) a.out_count[row] = kp.n;
+        if (a.out_status) a.out_status[row] = ST_OK;
+        if (a.seen_bits && tok >= 0) atomicOr(&a.seen_bits[row * a.seen_bits_stride + (tok >> 5)], 1u << (tok & 31));
+      }
+    }
+    return;
+  }
+  Kept kept = {0, 0.0f, 0};
+  int64_t token = -1;
+  if (dense && status == ST_OK && !general) {
+    const float dv = a.dense_mode == DENSE_SCORES ? NEG : 0.0f;
+    for (int64_t i = tid; i < V; i += NT) a.out_dense[row * a.dense_stride + i] = dv;
+    __syncthreads();
+  }
+  if (status == ST_OK && !general) {
+    if (m <= 64) {
+      if (warp == 0) {
+        kept = warp_finish<2>(a, fv, fi, m, uu, &token, kidx, kval);
+        if (lane == 0) {
+          bs.flag2 = kept.n;
+          bs.fval = kept.M;
+          bs.u64a = kept.tot;
+        }
+      }
+      __syncthreads();
+      kept.n = bs.flag2;
+      kept.M = bs.fval;
+      kept.tot = bs.u64a;
+    } else {
+      kept = leader_fast<NT>(a, bs, fv, fi, m, sval, sidx, Wb, Pb, kidx, kval);
+      token = draw_kept<NT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(sh.cval));
+    }
+    const float Sf = fix_to_float(kept.tot);
+    for (int j = tid; j < kept.n; j += NT) {
+      const float p = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kept.M)), Sf);
+      if (j < a.out_cap) {
+        if (a.out_idx) a.out_idx[row * a.out_cap + j] = kidx[j];
+        if (a.out_prob) a.out_prob[row * a.out_cap + j] = p;
+        if (a.out_score) a.out_score[row * a.out_cap + j] = kval[j];
+      }
+      if (dense) a.out_dense[row * a.dense_stride + kidx[j]] = a.dense_mode == DENSE_SCORES ? kval[j] : p;
+    }
+  } else if (general) {
+    auto seen = [&](int64_t i) -> bool { return (bits[i >> 5] >> (i & 31)) & 1u; };
+    auto emit = [&](int pos, int idx, float val, float Sf, float M) {
+      if (pos < a.out_cap) {
+        if (a.out_idx) a.out_idx[row * a.out_cap + pos] = idx;
+        if (a.out_prob) a.out_prob[row * a.out_cap + pos] = __fdiv_rn(sv_exp(__fsub_rn(val, M)), Sf);
+        if (a.out_score) a.out_score[row * a.out_cap + pos] = val;
+      }
+    };
+    kept = leader_slow<NT, TIn, MODE_SAMPLE>(a, bs, reinterpret_cast<unsigned char*>(sh.cval), row, 0.0f, 0.0f, uu,
+                                             &token, seen, emit);
+  } else if (dense) {
+    const float dv = a.dense_mode == DENSE_SCORES ? NEG : 0.0f;
+    for (int64_t i = tid; i < V; i += NT) a.out_dense[row * a.dense_stride + i] = dv;
+  }
+  if (tid == 0) {
+    a.out_token[row] = status == ST_OK ? token : -1;
+    if (a.out_count) a.out_count[row] = kept.n;
+    if (a.out_status) a.out_status[row] = status;
+    if (status == ST_OK && a.seen_bits && token >= 0)
+      atomicOr(&a.seen_bits[row * a.seen_bits_stride + (token >> 5)], 1u << (token & 31));
   }
 }
 
-template <typename TIn>
-cudaError_t launch_stream_t(const RowArgs& a, size_t smem, cudaStream_t stream) {
-  auto kern = stream_kernel<TIn>;
+// Threads per row: enough warps in flight over the whole GPU (about 32 per SM)
+// whatever the row count.
+int threads_for(int rows, int sms) {
+  if (rows >= sms * 6) return 128;
+  if (rows >= sms * 3) return 256;
+  return 512;
+}
+
+template <typename TIn, int NT>
+cudaError_t launch_nt(const RowArgs& a, size_t smem, cudaStream_t stream, int dev) {
+  auto kern = stream_kernel<TIn, NT>;
   static int configured[64] = {0};
-  static int slots[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_limit_stream());
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-    slots[dev] = kCtasPerSm * sms;
     configured[dev] = 1;
   }
-  const int grid = a.rows < slots[dev] ? a.rows : slots[dev];
-  kern<<<grid, SNT, smem, stream>>>(a);
+  kern<<<a.rows, NT, smem + static_bytes(NT), stream>>>(a);
   return cudaGetLastError();
+}
+
+template <typename TIn>
+cudaError_t launch_stream_t(const RowArgs& a, size_t smem, cudaStream_t stream) {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!sms[dev]) {
+    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  switch (threads_for(a.rows, sms[dev])) {
+    case 128: return launch_nt<TIn, 128>(a, smem, stream, dev);
+    case 256: return launch_nt<TIn, 256>(a, smem, stream, dev);
+    default: return launch_nt<TIn, 512>(a, smem, stream, dev);
+  }
 }
 
 }  // namespace
 
-// Dynamic shared memory of the streaming kernel for a vocabulary, or 0 when it
-// would not leave room for its CTAs per SM.
+// Shared memory of the batched kernel beyond its largest static layout (the row's
+// seen bitmap), or 0 when the row's bitmap would leave too little room for
+// several CTAs per SM (the cluster kernel then takes the rows).
 size_t stream_smem_bytes(int64_t vocab) {
-  const size_t s = kStaticBytes + (size_t)SBUF * SCHUNK + bitmap_bytes(vocab);
-  return s <= kSmemCap ? s : 0;
+  const size_t s = bitmap_bytes(vocab);
+  return s + static_bytes(512) <= 96 * 1024 ? s : 0;
 }
 
 cudaError_t launch_stream(const RowArgs& a, size_t smem, cudaStream_t stream) {

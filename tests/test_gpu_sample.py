@@ -302,14 +302,14 @@ def test_cfg4_full_size_against_oracle(sv, path):
         assert np.all(np.diff(got["idx"][r, :n]) > 0)
 
 
-@pytest.mark.parametrize("vocab,dtype,dense", [(5000, torch.float32, True), (49152, torch.float16, False),
-                                               (12345, torch.bfloat16, True)])
-def test_stream_more_rows_than_ctas(sv, vocab, dtype, dense):
-    """More rows than the streaming kernel has resident CTAs, so CTAs work through
-    several rows each (the ring runs ahead across row boundaries); random settings,
-    bit-exact against the oracle."""
+@pytest.mark.parametrize("vocab,dtype,dense,per_sm", [(5000, torch.float32, True, 7.05), (49152, torch.float16, False, 3.1),
+                                                      (12345, torch.bfloat16, True, 0.7), (49157, torch.float32, False, 6.2)])
+def test_stream_row_counts(sv, vocab, dtype, dense, per_sm):
+    """The batched kernel at row counts that pick each of its CTA sizes (128, 256
+    and 512 threads per row) and at more rows than fit the GPU at once; random
+    settings, bit-exact against the oracle."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    rows = 3 * sms + 7
+    rows = int(per_sm * sms) + 3
     g = np.random.default_rng(vocab)
     x = (2 * g.standard_normal((rows, vocab))).astype(np.float32)
     x[::5, g.choice(vocab, 12, replace=False)] += 9.0
@@ -317,3 +317,24 @@ def test_stream_more_rows_than_ctas(sv, vocab, dtype, dense):
     ids = g.integers(0, vocab, (rows, 300))
     got, ref = run_both(sv, x, u, ids=ids, T=1.3, p=0.85, dtype=dtype, dense=dense, cap=96, path="stream")
     assert_same(got, ref, dense=dense)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shift", [1, 3, 7, 13])
+def test_stream_row_offsets(sv, dtype, shift):
+    """Rows that start at every kind of offset from the 32-byte grid (a view into
+    a larger buffer with an odd row stride), so the first and last units of each
+    row are partial; bit-exact against the oracle."""
+    g = np.random.default_rng(100 + shift)
+    rows, V, stride = 70, 7001, 7001 + shift
+    buf = (2 * g.standard_normal(rows * stride + 64)).astype(np.float32)
+    full = to_dev(buf).to(dtype)
+    x = full[shift:shift + rows * stride].reshape(rows, stride)[:, :V]
+    ids = g.integers(0, V, (rows, 200))
+    u = to_dev(g.random(rows).astype(np.float32))
+    out = sv.sample_step(x, u, history=to_dev(ids.astype(np.int32)), out_capacity=64, path="stream")
+    torch.cuda.synchronize()
+    xf = x.float().cpu().numpy()
+    ref = O.sample(xf, u.cpu().numpy(), ids=ids, cap=64)
+    got = {k: v.cpu().numpy() for k, v in out.items()}
+    assert_same(got, ref, dense=False)
