@@ -16,11 +16,12 @@ resident in HBM; `e2e` is the same metric through the C ABI from pinned host
 buffers (host->device copies of logits, histories and uniforms and the
 device->host read of the tokens inside the timed region); `roofline` relates the
 kernel's algorithmic bytes to the measured HBM copy bandwidth; `cpu_baseline`
-times the CPU port of the reference algorithm (oracle/) on a bounded sample.
+times the reference's own chain in torch (oracle/torch_chain.py) on this host's
+cores on a bounded sample, beside the C restatement (oracle/).
 `extras` holds the latency configs (1, 2, 3) and the loop guard (config 5).
 
---impl reference times only the CPU port of the reference's algorithm on this
-host's cores, on the same workload and metric (rank 0; other ranks exit).
+--impl reference times only the reference's chain in torch on this host's cores,
+on the same 1024-row workload and metric (rank 0; other ranks exit).
 """
 from __future__ import annotations
 
@@ -235,16 +236,24 @@ def cpu_port_rows_per_s(data, seconds=10.0, chunk=64, threads=0):
 
 
 def run_reference(args, rank):
+    """The reference's own CPU chain (oracle/torch_chain.py: its torch calls, in its
+    order, runtime_shared.py:170-202) on this host's cores, over the same 1024-row
+    workload per step; rank 0 alone runs and prints."""
     if rank != 0:
         return
-    data = cfg4(rows=256)
-    from oracle import oracle as O
+    import torch
+    from oracle import torch_chain as TC
+    data = cfg4()
     threads = os.cpu_count()
-    x, h, u = data["logits"], data["history"], data["uniforms"]
-    per_step = 256
+    torch.set_num_threads(threads)
+    x = torch.from_numpy(data["logits"])
+    seen0 = TC.seen_mask(data["history"], V)
+    g = torch.Generator().manual_seed(0)
 
     def step():
-        O.sample(x, u, ids=h, temperature=1.5, top_p=0.9, cap=0, threads=threads)
+        seen = seen0.clone()  # each step starts from the workload's histories
+        for r in range(0, ROWS, 64):  # 64 rows per call: the chain's best throughput here
+            TC.sample_step(x[r:r + 64], seen[r:r + 64], generator=g)
 
     for _ in range(args.warmup):
         step()
@@ -252,15 +261,53 @@ def run_reference(args, rank):
     for _ in range(args.steps):
         step()
     dt = time.perf_counter() - t0
-    value = per_step * args.steps / dt
-    sample = f"{per_step} rows of the workload per step (CPU port of runtime_shared.py:170-202, oracle/)"
+    value = ROWS * args.steps / dt
+    sample = (f"all {ROWS} rows of the workload per step, 64 rows per call: penalty, temperature, top-k, top-p, "
+              f"softmax and torch.multinomial in torch on {threads} host threads (runtime_shared.py:170-202)")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "rows_per_step": per_step, "vocab": V, "history": HIST},
-            "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+            "config": workload_config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "torch-restatement",
+                             "cpu": cpu_model(), "sample": sample},
             "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def workload_config(world):
+    """The `config` of both arms' lines."""
+    return {"workload": WORKLOAD, "rows_per_gpu": ROWS, "vocab": V, "history_ids": HIST,
+            "parallelism": f"row-sharded x{world}, no collective in the step",
+            "l2": "two alternating input sets of 218 MB each (> 126 MB L2)"}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline(host, seconds):
+    """The reference's chain in torch on all host threads and on one, plus the C
+    port of the reference algorithm (oracle/), each on a bounded sample."""
+    from oracle import torch_chain as TC
+    seen = TC.seen_mask(host["history"], V)
+    threads = os.cpu_count()
+    rps, rows, dt = TC.rows_per_s(host["logits"], seen, seconds=seconds, chunk=64, threads=threads)
+    rps1, rows1, dt1 = TC.rows_per_s(host["logits"], seen, seconds=min(seconds, 5.0), chunk=8, threads=1)
+    prt, prows, pdt = cpu_port_rows_per_s(host, seconds=min(seconds, 5.0))
+    return {"value": rps, "unit": "rows/s", "cores": threads, "kind": "torch-restatement", "cpu": cpu_model(),
+            "sample": f"{rows} rows of the workload in {dt:.1f} s, 64 rows per call: the reference's torch chain "
+                      f"(runtime_shared.py:170-202, oracle/torch_chain.py)",
+            "single_thread": {"value": rps1, "unit": "rows/s", "cores": 1,
+                              "sample": f"{rows1} rows in {dt1:.1f} s, 8 rows per call"},
+            "c_port": {"value": prt, "unit": "rows/s", "cores": threads, "kind": "port",
+                       "sample": f"{prows} rows in {pdt:.1f} s (oracle/ C restatement, OpenMP over rows)"}}
 
 
 # ------------------------------------------------------------------ our arm
@@ -371,20 +418,12 @@ def run_ours(args, rank, world, local_rank):
         extras.update(vocab_sharded_beam_extra(sv, dev, rank, world))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        rps, rows, dt = cpu_port_rows_per_s(sets[0]["host"], seconds=args.cpu_seconds)
-        cpu = {"value": rps, "unit": "rows/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{rows} rows of the workload in {dt:.1f} s (oracle/ C port, OpenMP over rows)"}
-        rps1, rows1, dt1 = cpu_port_rows_per_s(sets[0]["host"], seconds=min(args.cpu_seconds, 5.0), chunk=8,
-                                               threads=1)
-        cpu["single_thread"] = {"value": rps1, "unit": "rows/s", "cores": 1,
-                                "sample": f"{rows1} rows in {dt1:.1f} s on one thread"}
+        cpu = cpu_baseline(sets[0]["host"], args.cpu_seconds)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "vocab": V, "history_ids": HIST,
-                           "parallelism": f"row-sharded x{world}, no collective in the step",
-                           "l2": "two alternating input sets of 218 MB each (> 126 MB L2)"},
+                "config": workload_config(world),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": profiled_traffic(),
                              "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "

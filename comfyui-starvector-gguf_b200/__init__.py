@@ -5,7 +5,7 @@ Layout:
   build.py            nvcc build of libstarvector_sampling.so, in-tree
   _lib.py             ctypes binding of the C ABI (no fallback: a missing library raises)
   ops.py              torch-tensor wrappers: sample_step, beam_step, loop_guard, penalize, ...
-  runtime_shared.py   drop-in mirror of the reference's sampling API (generate_tokens & co.)
+  runtime_shared.py   drop-in for the reference's sampling functions (_sample, _beam_sample & co.)
   sharded.py          row-sharded and vocabulary-sharded multi-GPU sampling (torch.distributed)
 
 The directory name is not a Python identifier (it is a ComfyUI custom-node folder);

@@ -1,17 +1,17 @@
 // sv_stream.cu -- the batched row kernel (sm_100a): many independent rows.
 //
 // One CTA per row.  The row's logits stream straight into registers as 32-byte
-// units (256-bit non-caching loads; BU units per thread per batch, the CTA's batch
-// a contiguous NT*BU*32-byte span) through two register buffers used in turn, so
-// the next batch is always in flight while a warp works on the current one.
-// Nothing is staged in shared memory and no block barrier separates the batches.
+// units (256-bit non-caching loads; one unit per thread per batch, the CTA's batch
+// a contiguous NT*32-byte span) through a ring of RING register buffers, so
+// RING - 1 batches are in flight while a warp works on one.  The logits are not
+// staged in shared memory and no block barrier separates the batches.
 //
 // Per row (runtime_shared.py:200-202):
-//   1. the row's seen bitmap in shared memory, from the history (its ids loaded
-//      in one round while the first two batches of logits are prefetched into L2);
+//   1. the row's seen bitmap in shared memory, from the history (its ids fetched
+//      by one bulk copy while the first RING batches of logits are in flight);
 //   2. a first lower bound tau of the row's k-th largest penalised score: the
 //      exact k-th largest of the threads' maxima over the unseen elements of the
-//      first two batches (NT distinct elements, each at or below its penalised
+//      first RING batches (NT distinct elements, each at or below its penalised
 //      score);
 //   3. every batch: the unit maxima of the raw scores (the penalty never raises a
 //      score, so a unit below tau holds no candidate) and, for the rare units that
@@ -50,28 +50,41 @@ constexpr int CAP = 1024;    // candidate capacity per row (split evenly between
 constexpr int SFIN = 256;    // candidates the fast finishes take
 constexpr int SBINS = 256;   // bound histogram bins
 constexpr int RW = 8;        // growth of a warp's list between its bound recomputations
-constexpr int IDV = 8;       // 16-byte history vectors per thread per load round
-#ifndef SV_STREAM_PREFETCH
-#define SV_STREAM_PREFETCH 8
-#endif
-constexpr int PF0 = SV_STREAM_PREFETCH;  // batches prefetched into L2 while the bitmap is built
+
+// Bytes of the staging region: the row's history ids (bulk copy) at the start,
+// then the candidate lists, the hit queues and the finish input.
+__host__ __device__ constexpr int lists_bytes(int nt) {
+  return 8 * CAP + (nt / 32) * QCAP * 36 + 8 * SFIN;
+}
+constexpr int kIdStage = 16 * 1024;  // history bytes taken by one bulk copy
+__host__ __device__ constexpr int stage_bytes(int nt) {
+  return lists_bytes(nt) > kIdStage ? lists_bytes(nt) : kIdStage;
+}
 
 template <int NT>
 struct __align__(16) StreamShared {
+  static constexpr int NW = NT / 32;
   BlockScratch<NT> bs;
   __align__(16) unsigned int bins[SBINS];
-  float wsort[NT / 32][32];  // first bound: each warp's values, descending
-  int wcount[NT / 32];       // candidates each warp found
-  __align__(16) uint4 qdata[NT / 32][2 * QCAP];  // each warp's queued hit units (32 bytes each)
-  int qunit[NT / 32][QCAP];                      // and their unit numbers
-  float boot_kth;            // kk-th largest of the first bound's values
-  unsigned int tau_key;      // ordered key of the shared bound (atomicMax)
-  unsigned int rmax_key;     // ordered key of the row's largest raw score
+  float wsort[NW][32];  // first bound: each warp's values, descending
+  int wcount[NW];       // candidates each warp found
+  float boot_kth;       // kk-th largest of the first bound's values
+  unsigned int tau_key;   // ordered key of the shared bound (atomicMax)
+  unsigned int rmax_key;  // ordered key of the row's largest raw score
   int err;
-  __align__(16) float cval[CAP];  // candidates: penalised score, index; warp w owns
-  int cidx[CAP];                  // entries [w * CAP / warps, (w + 1) * CAP / warps)
-  __align__(16) float fv[SFIN];   // finish input: tempered score, index
-  int fi[SFIN];
+  int ccount[NW];              // candidates of each warp's list reaching the final bound
+  unsigned int mkey;           // ordered key of the largest tempered candidate
+  unsigned long long idbar;  // completion of the history bulk copy
+  __align__(128) unsigned char stage[stage_bytes(NT)];
+  // The lists, over the staging region once the history is marked: candidates
+  // (penalised score, index; warp w owns [w * CAP / NW, (w + 1) * CAP / NW)), each
+  // warp's queued hit units (32 bytes each) and their unit numbers, the finish input.
+  __device__ float* cval() { return reinterpret_cast<float*>(stage); }
+  __device__ int* cidx() { return reinterpret_cast<int*>(stage + 4 * CAP); }
+  __device__ uint4* qdata(int w) { return reinterpret_cast<uint4*>(stage + 8 * CAP) + w * 2 * QCAP; }
+  __device__ int* qunit(int w) { return reinterpret_cast<int*>(stage + 8 * CAP + NW * QCAP * 32) + w * QCAP; }
+  __device__ float* fv() { return reinterpret_cast<float*>(stage + 8 * CAP + NW * QCAP * 36); }
+  __device__ int* fi() { return reinterpret_cast<int*>(stage + 8 * CAP + NW * QCAP * 36 + 4 * SFIN); }
 };
 
 __host__ __device__ constexpr size_t static_bytes(int nt) {
@@ -146,14 +159,6 @@ __device__ __forceinline__ float unit_max(const uint32_t (&w)[8]) {
     const uint32_t q[8] = {p, 0, 0, 0, 0, 0, 0, 0};
     return max_nan(U::at(q, 0), U::at(q, 1));
   }
-}
-
-// L2 prefetch of bytes [lo, hi) of global memory, trimmed to 16-byte bounds.
-__device__ __forceinline__ void prefetch_l2(uintptr_t lo, uintptr_t hi) {
-  lo = (lo + 15) & ~uintptr_t(15);
-  hi &= ~uintptr_t(15);
-  if (hi <= lo) return;
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)(hi - lo)) : "memory");
 }
 
 // Seen bits of elements e0 .. e0+E-1 (indices outside [0, V) give 0).
@@ -252,18 +257,18 @@ __device__ __noinline__ int2 drain_queue(StreamShared<NT>* shp, const uint32_t* 
   StreamShared<NT>& sh = *shp;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned lt_mask = (1u << lane) - 1u;
-  float* wval = sh.cval + warp * CAPW;
-  int* widx = sh.cidx + warp * CAPW;
+  float* wval = sh.cval() + warp * CAPW;
+  int* widx = sh.cidx() + warp * CAPW;
   __syncwarp();  // the queue's stores are visible to the warp
   const float tc = shared_tau(sh, c.tau0);
   const bool have = lane < qn;
   uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   int u = 0;
   if (have) {
-    const uint4 p = sh.qdata[warp][2 * lane], q = sh.qdata[warp][2 * lane + 1];
+    const uint4 p = sh.qdata(warp)[2 * lane], q = sh.qdata(warp)[2 * lane + 1];
     w[0] = p.x; w[1] = p.y; w[2] = p.z; w[3] = p.w;
     w[4] = q.x; w[5] = q.y; w[6] = q.z; w[7] = q.w;
-    u = sh.qunit[warp][lane];
+    u = sh.qunit(warp)[lane];
   }
 #pragma unroll
   for (int e = 0; e < E; ++e) {
@@ -297,54 +302,128 @@ __device__ __noinline__ int2 drain_queue(StreamShared<NT>* shp, const uint32_t* 
   return make_int2(cnt, last);
 }
 
-// The row's history ids in 16-byte vectors, IDV per thread per load round.
-struct IdRound {
-  uint4 v[IDV];
+// Shared state of finish_small (over the hit queues, which are dead by then).
+struct SmallFin {
+  ulonglong2 kw[64];   // candidates: {(value key, index), weight}
+  ulonglong2 kw2[64];  // kept entries: {index, weight}
+  unsigned long long all, below, removed;
+  float thr;
+  int f0, r, hit, last;
 };
 
-// Marks vectors [q0, q0 + IDV * NT) of a row's ids (held in r) in the shared
-// bitmap; returns the ST_HISTORY error bit for ids outside [0, V).
+// The finish of a row with m <= 64 candidates (fv, fi: tempered scores and
+// indices) by the whole block, two threads per candidate: each pair finds its
+// candidate's position and inclusive prefix sum in the ascending (value, index)
+// order, then in the index order of the kept entries, each thread taking every
+// other candidate and the pair adding their halves with one shuffle.  The k-th
+// largest with ties (runtime_shared.py:180-181), top-p with `keep` (:182-186) and
+// the index-order draw use the same exact integer arithmetic as warp_finish and
+// leader_fast.  M is the largest candidate.  Returns the Kept summary, sets
+// *token and writes the kept list in index order to kidx / kval (which may alias
+// fi / fv).  Every thread of the block must call it.
 template <int NT>
-__device__ __forceinline__ int mark_round(const IdRound& r, int64_t q0, int64_t nv, int64_t L, int idb, int64_t V,
-                                          uint32_t* bits) {
-  int err = 0;
-  auto mark = [&](int64_t x) {
-    if ((uint64_t)x >= (uint64_t)V) {
-      err |= 1 << ST_HISTORY;
-    } else {
-      const uint32_t b = 1u << (x & 31);
-      uint32_t* w = &bits[x >> 5];
-      if (!(*w & b)) atomicOr(w, b);  // repeated ids mostly find their bit set
-    }
-  };
-#pragma unroll
-  for (int k = 0; k < IDV; ++k) {
-    const int64_t q = q0 + threadIdx.x + (int64_t)k * NT;
-    if (q >= nv) break;
-    const uint4 t = r.v[k];
-    if (idb == 4) {
-      const int32_t id[4] = {(int32_t)t.x, (int32_t)t.y, (int32_t)t.z, (int32_t)t.w};
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-        if (q * 4 + s < L) mark(id[s]);
-    } else {
-      mark((int64_t)(((uint64_t)t.y << 32) | t.x));
-      if (q * 2 + 1 < L) mark((int64_t)(((uint64_t)t.w << 32) | t.z));
+__device__ Kept finish_small(const RowArgs& a, const float* fv, const int* fi, int m, float M, float u,
+                             int64_t* token, int* kidx, float* kval, SmallFin& f) {
+  static_assert(NT >= 128, "two threads per candidate, 64 candidates");
+  constexpr unsigned FULL = 0xffffffffu;
+  const int tid = threadIdx.x;
+  const int j = tid >> 1, h = tid & 1;
+  const bool act = j < m;
+  const float NEG = Elem<float>::neg_inf();
+  float v = NEG;
+  int id = 0;
+  uint64_t key = ~0ull, e = 0;
+  if (act) {
+    v = fv[j];
+    id = fi[j];
+    key = ((uint64_t)ord_key(v) << 32) | (uint32_t)id;
+    e = fixw(sv_exp(__fsub_rn(v, M)));
+    if (h == 0) f.kw[j] = make_ulonglong2(key, e);
+  }
+  if (tid == 0) {
+    f.below = 0;
+    f.removed = 0;
+    f.thr = NEG;
+    f.f0 = 0;
+    f.r = 0;
+    f.hit = 0x7fffffff;
+    f.last = -1;
+  }
+  __syncthreads();
+  // Position and inclusive prefix sum in the ascending (value, index) order.
+  int rk = 0;
+  uint64_t S = 0;
+  if (act) {
+#pragma unroll 4
+    for (int i = h; i < m; i += 2) {
+      const ulonglong2 kw = f.kw[i];
+      rk += kw.x < key;
+      S += kw.x <= key ? kw.y : 0ull;
     }
   }
-  return err;
-}
-
-template <int NT>
-__device__ __forceinline__ void load_round(IdRound& r, const uint4* h, int64_t q0, int64_t nv) {
-#pragma unroll
-  for (int k = 0; k < IDV; ++k) {
-    const int64_t q = q0 + threadIdx.x + (int64_t)k * NT;
-    if (q < nv) r.v[k] = __ldg(h + q);
+  rk += __shfl_xor_sync(FULL, rk, 1);
+  S += __shfl_xor_sync(FULL, S, 1);
+  if (act && h == 0) {
+    if (m >= a.kk && rk == m - a.kk) f.thr = v;  // the k-th largest value
+    if (rk == m - 1) f.all = S;                  // the largest holds the whole mass
   }
+  __syncthreads();
+  const float thr = f.thr;
+  const bool in = act && v >= thr;  // ties with the k-th largest are kept
+  if (act && h == 0 && !in) {
+    atomicAdd(&f.f0, 1);
+    atomicAdd(&f.below, (unsigned long long)e);
+  }
+  __syncthreads();
+  const int f0 = f.f0, m1 = m - f0;
+  const uint64_t below = f.below, total = f.all - below;
+  // Top-p: the ascending prefix with mass <= floor(total * pthr) goes, never the
+  // last `keep`.
+  bool rm = false;
+  if (a.pthr > 0.0f && in) {
+    const uint64_t thrW = mulfloor(total, a.pthr);
+    const int cap = m1 - a.keep > 0 ? m1 - a.keep : 0;
+    rm = S - below <= thrW && rk - f0 < cap;
+    if (rm && h == 0) {
+      atomicAdd(&f.r, 1);
+      atomicMax(&f.removed, (unsigned long long)(S - below));
+    }
+  }
+  const bool q = in && !rm;
+  if (act && h == 0) f.kw2[j] = make_ulonglong2(q ? (uint64_t)(uint32_t)id : ~0ull, q ? e : 0ull);
+  __syncthreads();
+  Kept kp;
+  kp.n = m1 - f.r;
+  kp.M = M;
+  kp.tot = total - f.removed;
+  // Position and inclusive prefix sum in index order over the kept entries; the
+  // draw is the first index whose prefix exceeds floor(u * mass), else the last.
+  int p = 0;
+  uint64_t Q = 0;
+  if (act) {
+    const uint64_t ix = (uint32_t)id;
+#pragma unroll 4
+    for (int i = h; i < m; i += 2) {
+      const ulonglong2 kw = f.kw2[i];
+      p += kw.x < ix;
+      Q += kw.x <= ix ? kw.y : 0ull;
+    }
+  }
+  p += __shfl_xor_sync(FULL, p, 1);
+  Q += __shfl_xor_sync(FULL, Q, 1);
+  if (q && h == 0) {
+    if (Q > mulfloor(kp.tot, u)) atomicMin(&f.hit, id);
+    atomicMax(&f.last, id);
+    kidx[p] = id;
+    kval[p] = v;
+  }
+  __syncthreads();
+  *token = f.hit != 0x7fffffff ? f.hit : f.last;
+  return kp;
 }
 
-// The other history forms (unaligned ids, the packed bitmap, the bool mask).
+// The history forms the bulk copy does not take (ids that are unaligned or too
+// many for the staging region, the packed bitmap, the bool mask).
 template <int NT>
 __device__ __forceinline__ int mark_other(const RowArgs& a, int64_t row, int64_t V, uint32_t* bits) {
   const int tid = threadIdx.x;
@@ -395,6 +474,7 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
   constexpr int NWARPS = NT / 32;
   constexpr int CAPW = CAP / NWARPS;  // candidates per warp list
   constexpr int BATCH = NT * BU;      // units per CTA batch
+  static_assert(sizeof(SmallFin) <= NWARPS * QCAP * 32, "the small finish's state lies over the hit queues");
   constexpr unsigned FULL = 0xffffffffu;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float NEG = Elem<float>::neg_inf();
@@ -432,21 +512,25 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
     }
   };
 
-  // 0. the first batches on their way into L2; the history ids in flight.
-  if (tid == 0) {
-    const uintptr_t hi = b32 + (uintptr_t)PF0 * BATCH * UB;
-    prefetch_l2(gs, hi < ge ? hi : ge);
-  }
+  // 0. the first RING batches of logits in flight; the history ids follow by one
+  //    bulk copy into the staging region when they fit it (larger or unaligned
+  //    histories and the other history forms by plain loads).
   const bool ids_kind = a.hist_kind == HIST_IDS32 || a.hist_kind == HIST_IDS64;
   const int idb = a.hist_kind == HIST_IDS64 ? 8 : 4;
   const int64_t L = ids_kind ? hist_length(a, row) : 0;
-  const uint4* h4 = ids_kind ? reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(a.hist) +
-                                                              (size_t)row * a.hist_stride * idb)
-                             : nullptr;
-  const bool vec_ids = ids_kind && (reinterpret_cast<uintptr_t>(h4) & 15) == 0;
-  const int64_t nv = vec_ids ? (L * idb + 15) / 16 : 0;
-  IdRound idr;
-  if (vec_ids) load_round<NT>(idr, h4, 0, nv);
+  const unsigned char* hrow =
+      ids_kind ? reinterpret_cast<const unsigned char*>(a.hist) + (size_t)row * a.hist_stride * idb : nullptr;
+  const bool stage_ids = ids_kind && (reinterpret_cast<uintptr_t>(hrow) & 15) == 0 && L * idb <= kIdStage;
+  const uint32_t tma_bytes = stage_ids ? (uint32_t)((L * idb) & ~int64_t(15)) : 0u;
+  if (tid == 0) {
+    mbar_init(&sh.idbar, 1);
+    mbar_init_fence();
+  }
+  uint32_t w0[1][8], w1[1][8], w2[1][8], w3[1][8];
+  load_batch(w0, 0);
+  load_batch(w1, 1);
+  load_batch(w2, 2);
+  load_batch(w3, 3);
 
   // 1. seen bitmap.
   {
@@ -461,13 +545,44 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
     }
   }
   __syncthreads();
+  if (tid == 0 && tma_bytes) {
+    mbar_expect_tx(&sh.idbar, tma_bytes);
+    bulk_g2s(sh.stage, hrow, tma_bytes, &sh.idbar);
+  }
   {
     int e = 0;
-    if (vec_ids) {
-      e = mark_round<NT>(idr, 0, nv, L, idb, V, bits);
-      for (int64_t q0 = (int64_t)IDV * NT; q0 < nv; q0 += (int64_t)IDV * NT) {
-        load_round<NT>(idr, h4, q0, nv);
-        e |= mark_round<NT>(idr, q0, nv, L, idb, V, bits);
+    auto mark = [&](int64_t x) {
+      if ((uint64_t)x >= (uint64_t)V) {
+        e |= 1 << ST_HISTORY;
+      } else {
+        const uint32_t bm = 1u << (x & 31);
+        uint32_t* wd = &bits[x >> 5];
+        if (!(*wd & bm)) atomicOr(wd, bm);  // repeated ids mostly find their bit set
+      }
+    };
+    if (stage_ids) {
+      // The ids past the last whole 16 bytes (fewer than four) by plain loads.
+      const int64_t done = tma_bytes / idb;
+      if (tid < L - done) mark(hist_id(a, row, done + tid));
+      if (tma_bytes) {
+        if (!mbar_wait(&sh.idbar, 0)) {
+          e |= 1 << ST_TIMEOUT;
+          (void)mbar_wait(&sh.idbar, 0);  // let a late copy land before the region is reused
+        } else {
+          const uint4* st = reinterpret_cast<const uint4*>(sh.stage);
+          for (int q = tid; q < (int)(tma_bytes >> 4); q += NT) {
+            const uint4 t = st[q];
+            if (idb == 4) {
+              mark((int32_t)t.x);
+              mark((int32_t)t.y);
+              mark((int32_t)t.z);
+              mark((int32_t)t.w);
+            } else {
+              mark((int64_t)(((uint64_t)t.y << 32) | t.x));
+              mark((int64_t)(((uint64_t)t.w << 32) | t.z));
+            }
+          }
+        }
       }
     } else {
       e = mark_other<NT>(a, row, V, bits);
@@ -476,14 +591,8 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
   }
   __syncthreads();
 
-  // 2. the first RING batches (one unit per thread each); the first bound: the
-  //    kk-th largest of the threads' maxima over their unseen elements (in the
-  //    order value desc, warp, lane).
-  uint32_t w0[1][8], w1[1][8], w2[1][8], w3[1][8];
-  load_batch(w0, 0);
-  load_batch(w1, 1);
-  load_batch(w2, 2);
-  load_batch(w3, 3);
+  // 2. the first bound: the kk-th largest of the threads' maxima over the unseen
+  //    elements of the first RING batches (in the order value desc, warp, lane).
   float boot;
   {
     float g = NEG;
@@ -568,9 +677,9 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
       }
       if (hit) {
         const int pos = qn + __popc(bal & lt_mask);
-        sh.qdata[warp][2 * pos] = make_uint4(w[0][0], w[0][1], w[0][2], w[0][3]);
-        sh.qdata[warp][2 * pos + 1] = make_uint4(w[0][4], w[0][5], w[0][6], w[0][7]);
-        sh.qunit[warp][pos] = b * BATCH + tid;
+        sh.qdata(warp)[2 * pos] = make_uint4(w[0][0], w[0][1], w[0][2], w[0][3]);
+        sh.qdata(warp)[2 * pos + 1] = make_uint4(w[0][4], w[0][5], w[0][6], w[0][7]);
+        sh.qunit(warp)[pos] = b * BATCH + tid;
       }
       qn += n;
     }
@@ -605,7 +714,10 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
     if (rmx == rmx) atomicMax(&sh.rmax_key, ord_key(rmx));
     sh.wcount[warp] = cnt;
   }
-  if (tid == 0) bs.flag = 0;
+  if (tid == 0) {
+    bs.flag = 0;
+    sh.mkey = 0;
+  }
   __syncthreads();
   // The final bound from the complete bins (every warp computes the same value).
   const float tfin = fmaxf(shared_tau(sh, tau0), hist_bound(sh.bins, base_key, bin_shift, kk, T));
@@ -615,30 +727,30 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
   for (int ow = 0; ow < NWARPS; ++ow) overflow |= sh.wcount[ow] > CAPW;
   int status = sh.err ? first_err(sh.err) : ST_OK;
   bool general = status == ST_OK && a.force_slow;
-  float* fv = sh.fv;
-  int* fi = sh.fi;
+  float* fv = sh.fv();
+  int* fi = sh.fi();
   // Finish scratch in the candidate lists (consumed by then).
-  float* sval = sh.cval;
-  int* sidx = reinterpret_cast<int*>(sh.cval + SFIN);
-  uint64_t* Wb = reinterpret_cast<uint64_t*>(sh.cval + 2 * SFIN);
-  uint64_t* Pb = reinterpret_cast<uint64_t*>(sh.cidx);
-  int* kidx = reinterpret_cast<int*>(sh.cidx) + 2 * SFIN;
-  float* kval = reinterpret_cast<float*>(sh.cidx);
+  float* sval = sh.cval();
+  int* sidx = reinterpret_cast<int*>(sh.cval() + SFIN);
+  uint64_t* Wb = reinterpret_cast<uint64_t*>(sh.cval() + 2 * SFIN);
+  uint64_t* Pb = reinterpret_cast<uint64_t*>(sh.cidx());
+  int* kidx = sh.cidx() + 2 * SFIN;
+  float* kval = reinterpret_cast<float*>(sh.cidx());
   int m = 0;
   if (status == ST_OK && !general) {
     // The candidates whose penalised score reaches the final bound, tempered.
-    // When a list overflowed, the row is read again (from L2 or HBM).
-    int bad = 0;
-    auto take = [&](int i, float x) {
-      const float tx = temper(x, T);
-      bad |= tx == PINF;
-      const int at = atomicAdd(&bs.flag, 1);
-      if (at < SFIN) {
-        fv[at] = tx;
-        fi[at] = i;
-      }
-    };
     if (overflow) {
+      // A list overflowed: the row is read again (from L2 or HBM).
+      int bad = 0;
+      auto take = [&](int i, float x) {
+        const float tx = temper(x, T);
+        bad |= tx == PINF;
+        const int at = atomicAdd(&bs.flag, 1);
+        if (at < SFIN) {
+          fv[at] = tx;
+          fi[at] = i;
+        }
+      };
       for (int64_t i = tid; i < V; i += NT) {
         float x = Elem<TIn>::load(rowp + i);
         if (x >= tfin) {
@@ -646,19 +758,57 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
           if (x >= tfin) take((int)i, x);
         }
       }
+      if (bad) atomicOr(&sh.err, 1 << ST_POSINF);
+      __syncthreads();
+      m = bs.flag;
+      if (sh.err) status = first_err(sh.err);
+      __syncthreads();
     } else {
-      for (int q = tid; q < CAP; q += NT) {
-        if (q % CAPW < sh.wcount[q / CAPW]) {
-          const float x = sh.cval[q];
-          if (x >= tfin) take(sh.cidx[q], x);
-        }
+      // Each warp compacts its own list: counts first, then every warp writes its
+      // entries after the lists before it (the finish input is ordered by warp
+      // list, then by position in the list).
+      const int n = sh.wcount[warp];
+      const float* lv = sh.cval() + warp * CAPW;
+      const int* li = sh.cidx() + warp * CAPW;
+      int c = 0;
+      bool bad = false;
+      float mx = NEG;
+      for (int b0 = 0; b0 < n; b0 += 32) {
+        const float x = b0 + lane < n ? lv[b0 + lane] : NEG;
+        const bool pass = x >= tfin;
+        const float tx = pass ? temper(x, T) : NEG;
+        bad |= tx == PINF;
+        mx = fmaxf(mx, tx);
+        c += __popc(__ballot_sync(FULL, pass));
       }
+      mx = warp_max_nan(mx);
+      bad = __any_sync(FULL, bad);
+      if (lane == 0) {
+        sh.ccount[warp] = c;
+        if (bad) atomicOr(&sh.err, 1 << ST_POSINF);
+        if (mx > NEG) atomicMax(&sh.mkey, ord_key(mx));
+      }
+      __syncthreads();
+      int off = 0;
+#pragma unroll
+      for (int ow = 0; ow < NWARPS; ++ow) {
+        if (ow < warp) off += sh.ccount[ow];
+        m += sh.ccount[ow];
+      }
+      for (int b0 = 0; b0 < n; b0 += 32) {
+        const float x = b0 + lane < n ? lv[b0 + lane] : NEG;
+        const bool pass = x >= tfin;
+        const unsigned bal = __ballot_sync(FULL, pass);
+        const int pos = off + __popc(bal & lt_mask);
+        if (pass && pos < SFIN) {
+          fv[pos] = temper(x, T);
+          fi[pos] = li[b0 + lane];
+        }
+        off += __popc(bal);
+      }
+      if (sh.err) status = first_err(sh.err);
+      __syncthreads();
     }
-    if (bad) atomicOr(&sh.err, 1 << ST_POSINF);
-    __syncthreads();
-    m = bs.flag;
-    if (sh.err) status = first_err(sh.err);
-    __syncthreads();
     if (m > SFIN) general = status == ST_OK;
   }
   if (general && temper(key_to_float(sh.rmax_key), T) == PINF) {
@@ -676,23 +826,24 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
   }
   if (status == ST_OK && !general && m == 0) status = ST_ALLNEGINF;
   const bool dense = a.out_dense && a.dense_mode != DENSE_NONE;
-  if (status == ST_OK && !general && m <= 64 && !dense) {
-    // Common case: warp 0 finishes the row in registers.
-    if (warp == 0) {
-      int64_t tok = -1;
-      const Kept kp = warp_finish<2>(a, fv, fi, m, uu, &tok, kidx, kval);
-      const float Sf = fix_to_float(kp.tot);
-      for (int j = lane; j < kp.n && j < a.out_cap; j += 32) {
-        if (a.out_idx) a.out_idx[row * a.out_cap + j] = kidx[j];
-        if (a.out_prob) a.out_prob[row * a.out_cap + j] = __fdiv_rn(sv_exp(__fsub_rn(kval[j], kp.M)), Sf);
-        if (a.out_score) a.out_score[row * a.out_cap + j] = kval[j];
-      }
-      if (lane == 0) {
-        a.out_token[row] = tok;
-        if (a.out_count) a.out_count[row] = kp.n;
-        if (a.out_status) a.out_status[row] = ST_OK;
-        if (a.seen_bits && tok >= 0) atomicOr(&a.seen_bits[row * a.seen_bits_stride + (tok >> 5)], 1u << (tok & 31));
-      }
+  if (status == ST_OK && !general && m <= 64 && !dense && !overflow) {
+    // Common case: the block finishes the row, two threads per candidate; its
+    // scratch is the hit queues (dead by now) and the kept list goes over the
+    // finish input.
+    int64_t tok = -1;
+    const Kept kp = finish_small<NT>(a, fv, fi, m, key_to_float(sh.mkey), uu, &tok, fi, fv,
+                                     *reinterpret_cast<SmallFin*>(sh.qdata(0)));
+    const float Sf = fix_to_float(kp.tot);
+    for (int j = tid; j < kp.n && j < a.out_cap; j += NT) {
+      if (a.out_idx) a.out_idx[row * a.out_cap + j] = fi[j];
+      if (a.out_prob) a.out_prob[row * a.out_cap + j] = __fdiv_rn(sv_exp(__fsub_rn(fv[j], kp.M)), Sf);
+      if (a.out_score) a.out_score[row * a.out_cap + j] = fv[j];
+    }
+    if (tid == 0) {
+      a.out_token[row] = tok;
+      if (a.out_count) a.out_count[row] = kp.n;
+      if (a.out_status) a.out_status[row] = ST_OK;
+      if (a.seen_bits && tok >= 0) atomicOr(&a.seen_bits[row * a.seen_bits_stride + (tok >> 5)], 1u << (tok & 31));
     }
     return;
   }
@@ -719,7 +870,7 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
       kept.tot = bs.u64a;
     } else {
       kept = leader_fast<NT>(a, bs, fv, fi, m, sval, sidx, Wb, Pb, kidx, kval);
-      token = draw_kept<NT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(sh.cval));
+      token = draw_kept<NT>(bs, kidx, kval, kept, uu, reinterpret_cast<uint64_t*>(sh.cval()));
     }
     const float Sf = fix_to_float(kept.tot);
     for (int j = tid; j < kept.n; j += NT) {
@@ -740,7 +891,7 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
         if (a.out_score) a.out_score[row * a.out_cap + pos] = val;
       }
     };
-    kept = leader_slow<NT, TIn, MODE_SAMPLE>(a, bs, reinterpret_cast<unsigned char*>(sh.cval), row, 0.0f, 0.0f, uu,
+    kept = leader_slow<NT, TIn, MODE_SAMPLE>(a, bs, reinterpret_cast<unsigned char*>(sh.cval()), row, 0.0f, 0.0f, uu,
                                              &token, seen, emit);
   } else if (dense) {
     const float dv = a.dense_mode == DENSE_SCORES ? NEG : 0.0f;

@@ -1,10 +1,13 @@
-"""Drop-in for the sampling part of ComfyUI-StarVector-GGUF's runtime_shared.py.
+"""Drop-in for the sampling step of ComfyUI-StarVector-GGUF's runtime_shared.py.
 
-Same names, arguments, return values and errors as the reference's sampling API
-(runtime_shared.py:147-342): the constants, `_repeating`, `_penalize`, `_warp`,
-`_ends`, `_sample`, `_beam_sample` and `generate_tokens`.  The decoder protocol is
-unchanged (`context`, `embed(ids)`, `prefill(embeddings, rows, capacity)` returning
-a decoding object with `step(tokens)` / `reorder(parents)` plus the first logits).
+Same names, arguments, return values and errors as the reference's sampling
+functions (runtime_shared.py:147-265): the constants, `_repeating`, `_penalize`,
+`_warp`, `_ends`, `_sample` and `_beam_sample`.  The reference's own
+`generate_tokens` (:268-342) stays in use: it calls `_sample` / `_beam_sample`
+through its module's globals, and `install(module)` rebinds those names (and
+`_repeating`, `_penalize`, `_warp`) to the functions here.  The decoder protocol is
+unchanged (`prefill(embeddings, rows, capacity)` returning a decoding object with
+`step(tokens)` / `reorder(parents)` plus the first logits).
 
 What changes is where the per-token sampling step runs: one fused sm_100a kernel
 per step (penalty from an on-device seen bitmap, temperature, top-k, top-p,
@@ -17,9 +20,6 @@ for the same seed.  Logits must live on a CUDA device.
 """
 from __future__ import annotations
 
-import logging
-from time import perf_counter
-
 import torch
 
 from . import _lib as L
@@ -31,8 +31,6 @@ REPETITION_PENALTY = 3.1
 LENGTH_PENALTY = -1.0
 LOOP_WINDOW = 64
 LOOP_REPEATS = 3
-
-logger = logging.getLogger(__name__)
 
 
 def _raise_status(status: int) -> None:
@@ -78,20 +76,16 @@ def _ends(tokens, stop_ids, eos_id):
 
 
 class _TokenHistory:
-    """Device copy of each row's generated tokens, for the loop guard."""
+    """Device copy of each row's generated tokens (int64), for the loop guard.  The
+    sampling kernel writes each step's token straight into its slot."""
 
     def __init__(self, rows, capacity, device):
-        self.ids = torch.zeros((rows, max(capacity, 1)), dtype=torch.int32, device=device)
-        self.spare = torch.empty_like(self.ids)
+        self.ids = torch.zeros((rows, max(capacity, 1)), dtype=torch.int64, device=device)
         self.length = 0
 
-    def append(self, tokens):
-        self.ids[:, self.length].copy_(tokens)
-        self.length += 1
-
-    def reorder(self, parents):
-        torch.index_select(self.ids, 0, parents, out=self.spare)
-        self.ids, self.spare = self.spare, self.ids
+    def slot(self, step):
+        """Row 0's slot of a step, as the kernel's token output."""
+        return self.ids[0, step:step + 1]
 
     def repeating(self, row=0, length=None):
         length = self.length if length is None else length
@@ -128,12 +122,13 @@ def _sample(decoder, embeddings, max_new_tokens, temperature, top_p, stop_ids, e
     tokens = []
     synced = 0
     for step in range(max_new_tokens):
-        out["status"] = statuses[step:step + 1]  # the kernel writes each step's status in place
+        # The kernel writes the token into the history and the status in place.
+        out["token"] = history.slot(step)
+        out["status"] = statuses[step:step + 1]
         out = ops.sample_step(logits.reshape(1, vocab), uniforms[step], seen_bits=seen, temperature=temperature,
                               top_p=top_p, top_k=TOP_K, keep=1, repetition_penalty=REPETITION_PENALTY,
                               update_seen_bits=seen, out=out)
-        token = out["token"]
-        history.append(token)
+        history.length = step + 1
         if step % _SYNC_EVERY == _SYNC_EVERY - 1 or step + 1 == max_new_tokens:
             block = history.ids[0, synced:step + 1].tolist()
             block_status = statuses[synced:step + 1].tolist()
@@ -148,7 +143,9 @@ def _sample(decoder, embeddings, max_new_tokens, temperature, top_p, stop_ids, e
                     return tokens, 'repetition'
             synced = step + 1
         if step + 1 < max_new_tokens:
-            logits = decoding.step(token)
+            # A failed step's token is -1 until the host reads the block and raises;
+            # the decoder is fed token 0 for it, so it only ever sees valid ids.
+            logits = decoding.step(out["token"].clamp_min(0))
     return tokens, 'token_limit'
 
 
@@ -220,67 +217,8 @@ def _beam_sample(decoder, embeddings, max_new_tokens, temperature, top_p, beams,
     return best, ('token_limit' if len(best) == max_new_tokens and not _ends(best, stop_ids, eos_id) else 'stop')
 
 
-def generate_tokens(decoder, tokenizer, prefix, max_new_tokens=4096, temperature=1.5, top_p=0.9, seed=0,
-                    num_beams=2, loop_guard=True, progress_callback=None):
-    """Generate SVG with StarVector's original sampling on `decoder` (runtime_shared.py:268-342).
-
-    `decoder` provides `context`, `embed(ids)` and `prefill(embeddings, rows, capacity)`,
-    which returns a decoding object with `step(tokens)` and `reorder(parents)` plus the
-    first logits.  One sequence is returned.
-    """
-    if prefix.ndim != 3 or prefix.shape[0] != 1:
-        raise ValueError("Expected one image embedding sequence [1,T,H]")
-    if max_new_tokens < 1:
-        raise ValueError("max_new_tokens must be positive")
-    if temperature <= 0:
-        raise ValueError("Sampling requires temperature > 0")
-    if not 0 < top_p <= 1:
-        raise ValueError("top_p must be in (0, 1]")
-    if not isinstance(num_beams, int) or not 1 <= num_beams <= 8:
-        raise ValueError("num_beams must be an integer between 1 and 8")
-    device = prefix.device
-    prompt_ids = tokenizer.encode("<svg")
-    stop_ids = tokenizer.encode("</svg>")
-    if not prompt_ids or not stop_ids:
-        raise ValueError("Tokenizer cannot encode SVG control tokens")
-    context = decoder.context
-    prefix_length = prefix.shape[1] + len(prompt_ids)
-    available = context - prefix_length
-    if available < 1:
-        raise ValueError(f"Generation exceeds context size {context}: "
-                         f"prefix={prefix.shape[1]}, prompt={len(prompt_ids)}")
-    requested_new_tokens = int(max_new_tokens)
-    max_new_tokens = min(requested_new_tokens, available)
-    logger.info("StarVector: context=%d, image prefix=%d, SVG prompt=%d, requested max_new_tokens=%d, "
-                "effective max_new_tokens=%d, top_k=%d, repetition_penalty=%s, loop_guard=%s", context,
-                prefix.shape[1], len(prompt_ids), requested_new_tokens, max_new_tokens, TOP_K, REPETITION_PENALTY,
-                loop_guard)
-    prompt = torch.tensor([prompt_ids], dtype=torch.long, device=device)
-    embeddings = torch.cat((prefix, decoder.embed(prompt).to(prefix.dtype)), dim=1)
-    on_step = progress_callback if progress_callback is not None else (lambda step: None)
-    cuda_devices = [device.index if device.index is not None else torch.cuda.current_device()] \
-        if device.type == "cuda" else []
-    started = perf_counter()
-    with torch.inference_mode(), torch.random.fork_rng(devices=cuda_devices):
-        torch.manual_seed(int(seed))
-        if num_beams == 1:
-            generated, reason = _sample(decoder, embeddings, max_new_tokens, float(temperature), float(top_p),
-                                        stop_ids, tokenizer.eos_token_id, loop_guard, on_step)
-        else:
-            generated, reason = _beam_sample(decoder, embeddings, max_new_tokens, float(temperature), float(top_p),
-                                             num_beams, stop_ids, tokenizer.eos_token_id, loop_guard, on_step)
-    svg = tokenizer.decode(prompt_ids + generated)
-    if not svg.startswith("<svg"):
-        raise RuntimeError("Generated text does not start with the SVG prompt")
-    elapsed = perf_counter() - started
-    has_terminator = svg.rstrip().endswith("</svg>")
-    logger.info("StarVector: decoded %d/%d tokens in %.2fs (%.2f tokens/s); beams=%d, stop=%s, "
-                "SVG terminator at end=%s", len(generated), max_new_tokens, elapsed,
-                len(generated) / max(elapsed, 1e-9), num_beams, reason, has_terminator)
-    if reason == "repetition":
-        logger.warning("StarVector: stopped after %d tokens because the model kept repeating the same output "
-                       "(loop guard)", len(generated))
-    elif not has_terminator:
-        logger.warning("StarVector: decoder stopped without a final </svg> (reason=%s, generated=%d/%d tokens); "
-                       "output tail=%r", reason, len(generated), max_new_tokens, svg[-160:])
-    return svg
+def install(module) -> None:
+    """Rebind the reference module's sampling functions to these (its own
+    `generate_tokens`, runtime_shared.py:268-342, then runs the kernels)."""
+    for name in ("_repeating", "_penalize", "_warp", "_sample", "_beam_sample"):
+        setattr(module, name, globals()[name])

@@ -1,8 +1,12 @@
 """The reference's generation-loop tests (tests/test_generation.py:52-122 of
-ComfyUI-StarVector-GGUF), run against the drop-in runtime_shared on CUDA.
+ComfyUI-StarVector-GGUF), run against the drop-in's _sample / _beam_sample on CUDA.
 
-The fake decoder makes one scripted token dominant (logit 200), so outcomes do
-not depend on the draw rule: the same assertions as the reference's must hold.
+The reference's generate_tokens (runtime_shared.py:268-342) stays the caller;
+`generate` below makes the same calls it does (prompt embeddings appended to the
+image prefix, max_new_tokens capped by the context, the seed set inside fork_rng,
+:301-319).  The fake decoder makes one scripted token dominant (logit 200), so
+outcomes do not depend on the draw rule: the same assertions as the reference's
+must hold.  The decoder also checks that it is only ever fed valid token ids.
 """
 import pytest
 import torch
@@ -42,7 +46,10 @@ class CudaScriptDecoder:
         return logits
 
     def step(self, tokens):
-        self.calls.append(("step", tokens.tolist()))
+        ids = tokens.tolist()
+        # An out-of-range id would be an embedding fault in a real decoder.
+        assert all(0 <= t < self.vocab for t in ids), ids
+        self.calls.append(("step", ids))
         self.step_index += 1
         return self._logits(tokens.shape[0])
 
@@ -56,48 +63,64 @@ def rs(sv):
     return importlib.import_module("starvector_b200.runtime_shared")
 
 
+def generate(rs, decoder, prefix, max_new_tokens=4096, num_beams=2, loop_guard=True, progress_callback=None,
+             seed=0):
+    """The drop-in's sampling loops called as the reference's generate_tokens calls
+    them; returns (decoded text, stop reason)."""
+    tok = TinyTokenizer()
+    prompt_ids, stop_ids = tok.encode("<svg"), tok.encode("</svg>")
+    max_new = min(int(max_new_tokens), decoder.context - prefix.shape[1] - len(prompt_ids))
+    embeddings = torch.cat((prefix, decoder.embed(torch.tensor([prompt_ids], device=DEV))), dim=1)
+    on_step = progress_callback if progress_callback is not None else (lambda step: None)
+    with torch.inference_mode(), torch.random.fork_rng(devices=[torch.cuda.current_device()]):
+        torch.manual_seed(seed)
+        if num_beams == 1:
+            generated, reason = rs._sample(decoder, embeddings, max_new, 1.5, 0.9, stop_ids, tok.eos_token_id,
+                                           loop_guard, on_step)
+        else:
+            generated, reason = rs._beam_sample(decoder, embeddings, max_new, 1.5, 0.9, num_beams, stop_ids,
+                                                tok.eos_token_id, loop_guard, on_step)
+    return tok.decode(prompt_ids + generated), reason
+
+
 @pytest.mark.parametrize("beams", [1, 2, 8])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
 def test_generates_until_svg_end(rs, beams, dtype):
     decoder = CudaScriptDecoder([7, 8, 3, 4, 9], dtype=dtype)
-    cpu_before, cuda_before = torch.get_rng_state(), torch.cuda.get_rng_state()
-    svg = rs.generate_tokens(decoder, TinyTokenizer(), torch.zeros(1, 8, 4, device=DEV), max_new_tokens=16,
-                             num_beams=beams)
+    svg, reason = generate(rs, decoder, torch.zeros(1, 8, 4, device=DEV), max_new_tokens=16, num_beams=beams)
     assert svg == "<svg 7 8 3 4"
+    assert reason == "stop"
     assert decoder.calls[0] == ("prefill", 10, beams, 26)
-    assert torch.equal(torch.get_rng_state(), cpu_before)
-    assert torch.equal(torch.cuda.get_rng_state(), cuda_before)
 
 
 def test_generation_emits_incremental_progress(rs):
     events = []
-    rs.generate_tokens(CudaScriptDecoder([7, 3, 4]), TinyTokenizer(), torch.zeros(1, 8, 4, device=DEV),
-                       max_new_tokens=8, num_beams=1, progress_callback=events.append)
+    generate(rs, CudaScriptDecoder([7, 3, 4]), torch.zeros(1, 8, 4, device=DEV), max_new_tokens=8, num_beams=1,
+             progress_callback=events.append)
     assert events == [1, 2, 3]
 
 
-def test_context_cap(rs, caplog):
+@pytest.mark.parametrize("beams", [1, 2])
+def test_token_limit(rs, beams):
     decoder = CudaScriptDecoder([7])
-    with caplog.at_level("INFO", logger=rs.__name__):
-        svg = rs.generate_tokens(decoder, TinyTokenizer(), torch.zeros(1, 34, 4, device=DEV), max_new_tokens=4096,
-                                 num_beams=1)
-    assert "requested max_new_tokens=4096, effective max_new_tokens=4" in caplog.text
+    svg, reason = generate(rs, decoder, torch.zeros(1, 34, 4, device=DEV), max_new_tokens=4096, num_beams=beams)
     assert svg == "<svg 7 7 7 7"
-    assert decoder.calls[0] == ("prefill", 36, 1, 40)
+    assert reason == "token_limit"
+    assert decoder.calls[0] == ("prefill", 36, beams, 40)
 
 
 @pytest.mark.parametrize("beams", [1, 2])
-def test_loop_guard_stops_repeated_output(rs, beams, caplog):
+def test_loop_guard_stops_repeated_output(rs, beams):
     script = list(range(5, 69)) * 20
-    with caplog.at_level("WARNING", logger=rs.__name__):
-        svg = rs.generate_tokens(CudaScriptDecoder(script, context=2000), TinyTokenizer(),
-                                 torch.zeros(1, 8, 4, device=DEV), max_new_tokens=1000, num_beams=beams)
+    svg, reason = generate(rs, CudaScriptDecoder(script, context=2000), torch.zeros(1, 8, 4, device=DEV),
+                           max_new_tokens=1000, num_beams=beams)
     generated = len(svg.split()) - 1
     assert 64 * 3 <= generated < 64 * 3 + 16
-    assert "loop guard" in caplog.text
-    svg = rs.generate_tokens(CudaScriptDecoder(script, context=2000), TinyTokenizer(),
-                             torch.zeros(1, 8, 4, device=DEV), max_new_tokens=1000, num_beams=beams, loop_guard=False)
+    assert reason == "repetition"
+    svg, reason = generate(rs, CudaScriptDecoder(script, context=2000), torch.zeros(1, 8, 4, device=DEV),
+                           max_new_tokens=1000, num_beams=beams, loop_guard=False)
     assert len(svg.split()) - 1 == 1000
+    assert reason == "token_limit"
 
 
 def test_processors_match_transformers(rs):
@@ -129,9 +152,10 @@ def test_stop_inside_a_read_block(rs):
     stops there, with the progress callback called once per step up to it."""
     events = []
     script = [7] * 19 + [3, 4] + [8] * 20
-    svg = rs.generate_tokens(CudaScriptDecoder(script), TinyTokenizer(), torch.zeros(1, 8, 4, device=DEV),
-                             max_new_tokens=30, num_beams=1, progress_callback=events.append)
+    svg, reason = generate(rs, CudaScriptDecoder(script), torch.zeros(1, 8, 4, device=DEV), max_new_tokens=30,
+                           num_beams=1, progress_callback=events.append)
     assert svg == "<svg" + " 7" * 19 + " 3 4"
+    assert reason == "stop"
     assert events == list(range(1, 22))
 
 
@@ -145,9 +169,13 @@ class NanAtStepDecoder(CudaScriptDecoder):
 
 def test_error_status_inside_a_read_block(rs):
     """A step whose logits hold a NaN raises the reference's error even though the
-    host reads the steps' statuses only once per 16 steps."""
+    host reads the steps' statuses only once per 16 steps; the decode steps issued
+    after the failed one inside the block are fed valid ids (the decoder asserts it)."""
     events = []
+    decoder = NanAtStepDecoder([7])
     with pytest.raises(RuntimeError, match="probability tensor contains"):
-        rs.generate_tokens(NanAtStepDecoder([7]), TinyTokenizer(), torch.zeros(1, 8, 4, device=DEV),
-                           max_new_tokens=30, num_beams=1, progress_callback=events.append)
+        generate(rs, decoder, torch.zeros(1, 8, 4, device=DEV), max_new_tokens=30, num_beams=1,
+                 progress_callback=events.append)
     assert events == list(range(1, 10))
+    fed = [c[1][0] for c in decoder.calls if c[0] == "step"]
+    assert fed == [7] * 9 + [0] + [7] * 5  # the failed step 9 is fed as token 0
