@@ -32,7 +32,8 @@ constexpr int kMaxDevices = 64;
 void* g_scratch_addr[kMaxDevices] = {};
 std::mutex g_scratch_mutex;
 
-// Device address of the scratch on the current device, looked up once per device.
+// Device address of the scratch on the current device, looked up once per device
+// and kept for the life of the process (it does not survive a device reset).
 cudaError_t scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -8,7 +8,7 @@
 //
 // Per row (runtime_shared.py:200-202):
 //   1. the row's seen bitmap in shared memory, from the history (its ids fetched
-//      by one bulk copy while the first RING batches of logits are in flight);
+//      by one bulk copy issued as the CTA starts);
 //   2. a first lower bound tau of the row's k-th largest penalised score: the
 //      exact k-th largest of the threads' maxima over the unseen elements of the
 //      first RING batches (NT distinct elements, each at or below its penalised
@@ -62,7 +62,7 @@ __host__ __device__ constexpr int stage_bytes(int nt) {
 }
 
 template <int NT>
-struct __align__(16) StreamShared {
+struct __align__(128) StreamShared {
   static constexpr int NW = NT / 32;
   BlockScratch<NT> bs;
   __align__(16) unsigned int bins[SBINS];
@@ -512,9 +512,10 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
     }
   };
 
-  // 0. the first RING batches of logits in flight; the history ids follow by one
-  //    bulk copy into the staging region when they fit it (larger or unaligned
-  //    histories and the other history forms by plain loads).
+  // 0. the history ids by one bulk copy into the staging region when they fit it
+  //    (larger or unaligned histories and the other history forms by plain loads).
+  //    The first logits are loaded once the bitmap is built: loads outstanding
+  //    during the bitmap build slow its shared-memory work.
   const bool ids_kind = a.hist_kind == HIST_IDS32 || a.hist_kind == HIST_IDS64;
   const int idb = a.hist_kind == HIST_IDS64 ? 8 : 4;
   const int64_t L = ids_kind ? hist_length(a, row) : 0;
@@ -524,13 +525,13 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
   const uint32_t tma_bytes = stage_ids ? (uint32_t)((L * idb) & ~int64_t(15)) : 0u;
   if (tid == 0) {
     mbar_init(&sh.idbar, 1);
-    mbar_init_fence();
+    fence_proxy_async_smem();  // the initialised barrier is visible to the bulk copy
+    if (tma_bytes) {
+      mbar_expect_tx(&sh.idbar, tma_bytes);
+      bulk_g2s(sh.stage, hrow, tma_bytes, &sh.idbar);
+    }
   }
   uint32_t w0[1][8], w1[1][8], w2[1][8], w3[1][8];
-  load_batch(w0, 0);
-  load_batch(w1, 1);
-  load_batch(w2, 2);
-  load_batch(w3, 3);
 
   // 1. seen bitmap.
   {
@@ -545,41 +546,46 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
     }
   }
   __syncthreads();
-  if (tid == 0 && tma_bytes) {
-    mbar_expect_tx(&sh.idbar, tma_bytes);
-    bulk_g2s(sh.stage, hrow, tma_bytes, &sh.idbar);
-  }
   {
     int e = 0;
-    auto mark = [&](int64_t x) {
-      if ((uint64_t)x >= (uint64_t)V) {
-        e |= 1 << ST_HISTORY;
-      } else {
-        const uint32_t bm = 1u << (x & 31);
-        uint32_t* wd = &bits[x >> 5];
-        if (!(*wd & bm)) atomicOr(wd, bm);  // repeated ids mostly find their bit set
-      }
-    };
     if (stage_ids) {
       // The ids past the last whole 16 bytes (fewer than four) by plain loads.
       const int64_t done = tma_bytes / idb;
-      if (tid < L - done) mark(hist_id(a, row, done + tid));
+      if (tid < L - done) {
+        const int64_t x = hist_id(a, row, done + tid);
+        if ((uint64_t)x >= (uint64_t)V) e |= 1 << ST_HISTORY;
+        else atomicOr(&bits[x >> 5], 1u << (x & 31));
+      }
       if (tma_bytes) {
-        if (!mbar_wait(&sh.idbar, 0)) {
+        if (!__all_sync(FULL, mbar_wait(&sh.idbar, 0))) {  // warp-uniform, for the reductions below
           e |= 1 << ST_TIMEOUT;
           (void)mbar_wait(&sh.idbar, 0);  // let a late copy land before the region is reused
         } else {
           const uint4* st = reinterpret_cast<const uint4*>(sh.stage);
-          for (int q = tid; q < (int)(tma_bytes >> 4); q += NT) {
-            const uint4 t = st[q];
-            if (idb == 4) {
-              mark((int32_t)t.x);
-              mark((int32_t)t.y);
-              mark((int32_t)t.z);
-              mark((int32_t)t.w);
+          const int nvec = (int)(tma_bytes >> 4);
+          const uint32_t uV = (uint32_t)V;
+          auto mark32 = [&](uint32_t x) {
+            if (x >= uV) {
+              e |= 1 << ST_HISTORY;
             } else {
-              mark((int64_t)(((uint64_t)t.y << 32) | t.x));
-              mark((int64_t)(((uint64_t)t.w << 32) | t.z));
+              const uint32_t bm = 1u << (x & 31);
+              uint32_t* wd = &bits[x >> 5];
+              if (!(*wd & bm)) atomicOr(wd, bm);
+            }
+          };
+          if (idb == 4) {
+            for (int q = tid; q < nvec; q += NT) {
+              const uint4 t = st[q];
+              mark32(t.x);
+              mark32(t.y);
+              mark32(t.z);
+              mark32(t.w);
+            }
+          } else {
+            for (int q = tid; q < nvec; q += NT) {
+              const uint4 t = st[q];
+              mark32(t.y ? ~0u : t.x);
+              mark32(t.w ? ~0u : t.z);
             }
           }
         }
@@ -593,6 +599,10 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
 
   // 2. the first bound: the kk-th largest of the threads' maxima over the unseen
   //    elements of the first RING batches (in the order value desc, warp, lane).
+  load_batch(w0, 0);
+  load_batch(w1, 1);
+  load_batch(w2, 2);
+  load_batch(w3, 3);
   float boot;
   {
     float g = NEG;

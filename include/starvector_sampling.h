@@ -146,8 +146,11 @@ int sv_beam_step(const void* logits, int32_t logits_dtype, int32_t beams, int32_
  * Limit: sv_beam_workspace_bytes(beams, vocab) <= 8 MiB, i.e. beams * vocab <=
  * 524271 (8 beams up to vocab 65533); larger calls return SV_E_NOALLOC_LIMIT.
  * The first call on a device looks up the array's device address (make it before
- * any stream capture).  Each call clears the array's header on `stream`.  All calls
- * share the array: calls that overlap on the GPU race.
+ * any stream capture) and keeps it for the life of the process: after
+ * cudaDeviceReset, or anything else that replaces the device's primary context,
+ * that address is stale, so the entry point must not be called again on that
+ * device.  Each call clears the array's header on `stream`.  All calls share the
+ * array: calls that overlap on the GPU race.
  */
 int sv_beam_step_noalloc(const void* logits, int32_t logits_dtype, int32_t beams, int32_t vocab,
                          int64_t logits_row_stride, const void* history, int32_t history_kind,

@@ -73,6 +73,8 @@ float orc_exp(float x)
     if (x < -104.0f) return 0.0f;
     float j = rintf(x * 1.44269502162933349609375f);
     int n = (int)j;
+    // ln 2 split in two floats, as SLEEF's single-precision L2Uf / L2Lf (Cody-Waite):
+    // the high part has few mantissa bits, so j times it is exact over the j used here.
     float r = fmaf(-j, 0.693145751953125f, x);
     r = fmaf(-j, 1.428606765330187045e-06f, r);
     float p = 1.98412698412698412698e-4f;

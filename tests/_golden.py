@@ -11,6 +11,7 @@ rounding or on tie order, which the north-star parity bar exempts:
 from __future__ import annotations
 
 import glob
+import hashlib
 import os
 
 import numpy as np
@@ -24,8 +25,46 @@ def load(name):
     z = np.load(os.path.join(GOLDEN, name + ".npz"))
     d = {k: z[k] for k in z.files}
     V = int(d["vocab"])
-    d["seen"] = np.unpackbits(d["seen"], axis=1)[:, :V].astype(bool)
+    if "gen" in d:
+        d.update(regenerate(d))
+    else:
+        d["seen"] = np.unpackbits(d["seen"], axis=1)[:, :V].astype(bool)
     return d
+
+
+def digest(*arrays):
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+def regenerate(d):
+    """Inputs of a full-size fixture from bench.py's seeded generators, checked
+    against the digest the generator script stored (tests/golden/make_golden.py)."""
+    import bench
+    gen, seed = str(d["gen"]), int(d["gen_seed"])
+    if gen == "cfg4":
+        w = bench.cfg4(seed=seed, rows=int(d["gen_rows"]))
+    elif gen == "cfg3":
+        w = bench.cfg3(seed=seed)
+    else:
+        raise ValueError(gen)
+    assert digest(w["logits"], w["history"]) == str(d["sha"]), f"{gen}: generator output changed"
+    V = int(d["vocab"])
+    seen = np.zeros((w["logits"].shape[0], V), bool)
+    for r, ids in enumerate(w["history"]):
+        seen[r, ids] = True
+    return dict(logits=w["logits"], seen=seen, history=w["history"])
+
+
+def cfg5_fixture():
+    """Config 5's tokens (regenerated, digest-checked) and the reference's verdicts."""
+    import bench
+    z = np.load(os.path.join(GOLDEN, "repeat_cfg5.npz"))
+    t = bench.cfg5_tokens(seed=int(z["gen_seed"]))
+    assert digest(t) == str(z["sha"]), "cfg5_tokens output changed"
+    return t, z["verdict"]
 
 
 def names(prefix):

@@ -1,6 +1,7 @@
 """Generate golden vectors by running the reference's own sampling functions.
 
-    python tests/golden/make_golden.py [/path/to/ComfyUI-StarVector-GGUF]
+    python tests/golden/make_golden.py --reference /path/to/ComfyUI-StarVector-GGUF [--only big]
+    (or with STARVECTOR_REF=/path/to/ComfyUI-StarVector-GGUF in the environment)
 
 Imports the unmodified reference (ComfyUI-StarVector-GGUF, runtime_shared.py) as
 the package `starvector_node`, the way its own tests do (tests/package_alias.py),
@@ -15,9 +16,17 @@ Fixtures:
   beam_<case>.npz  the beam step of runtime_shared.py:230-235: log_probs, the
                    softmax over beams*V and count_nonzero, stored sparse.
   repeat.npz       _repeating verdicts (runtime_shared.py:156-167).
+The full-size BASELINE configurations (a 16-row slice of config 4 with Zipf
+histories, config 3's eight bf16 beams at V=49152, config 5's 256 loop-guard rows
+of 16384 tokens) are too large to store: their fixtures (proc_cfg4z, beam_cfg3,
+repeat_cfg5) hold the reference's outputs plus the generator (bench.py's seeded
+workload functions), its arguments and a SHA-256 of the generated inputs, which
+the tests regenerate and check.
 """
 from __future__ import annotations
 
+import argparse
+import hashlib
 import os
 import sys
 import types
@@ -26,7 +35,15 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
 V_BIG = 49152
+
+
+def digest(*arrays):
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
 
 
 def load_reference(path):
@@ -64,7 +81,7 @@ def sparse_rows(dense, keep_mask):
     return np.array(offs, np.int64), np.concatenate(idx), np.concatenate(vals)
 
 
-def proc_case(rs, name, logits, seen, temperature, top_p, keep, extra=None):
+def proc_case(rs, name, logits, seen, temperature, top_p, keep, extra=None, store_inputs=True):
     x = torch.from_numpy(logits.astype(np.float32))
     s = torch.from_numpy(seen)
     warped = rs._warp(rs._penalize(x, s), temperature, top_p, keep)
@@ -74,16 +91,17 @@ def proc_case(rs, name, logits, seen, temperature, top_p, keep, extra=None):
     kept = np.isfinite(w)
     offs, idx, vals = sparse_rows(w, kept)
     _, _, pv = sparse_rows(p, kept)
-    out = dict(logits=logits.astype(np.float32), seen=np.packbits(seen, axis=1), vocab=np.int64(seen.shape[1]),
-               temperature=np.float64(temperature), top_p=np.float64(top_p), keep=np.int64(keep),
-               offs=offs, idx=idx, val=vals, prob=pv)
+    out = dict(vocab=np.int64(seen.shape[1]), temperature=np.float64(temperature), top_p=np.float64(top_p),
+               keep=np.int64(keep), offs=offs, idx=idx, val=vals, prob=pv)
+    if store_inputs:
+        out.update(logits=logits.astype(np.float32), seen=np.packbits(seen, axis=1))
     if extra:
         out.update(extra)
     np.savez_compressed(os.path.join(HERE, f"proc_{name}.npz"), **out)
     print(f"proc_{name}: rows={logits.shape[0]} V={logits.shape[1]} kept={np.diff(offs).tolist()[:8]}")
 
 
-def beam_case(rs, name, logits, seen, running, temperature=1.5, top_p=0.9):
+def beam_case(rs, name, logits, seen, running, temperature=1.5, top_p=0.9, extra=None):
     x = torch.from_numpy(logits.astype(np.float32))
     s = torch.from_numpy(seen)
     B, V = x.shape
@@ -97,17 +115,47 @@ def beam_case(rs, name, logits, seen, running, temperature=1.5, top_p=0.9):
     offs, idx, vals = sparse_rows(lp, kept)
     pf = probs.numpy()[0]
     nz = np.nonzero(pf)[0]
-    np.savez_compressed(os.path.join(HERE, f"beam_{name}.npz"),
-                        logits=logits.astype(np.float32), seen=np.packbits(seen, axis=1), vocab=np.int64(V),
-                        running=np.asarray(running, np.float64), temperature=np.float64(temperature),
-                        top_p=np.float64(top_p), offs=offs, idx=idx, val=vals,
-                        prob_idx=nz.astype(np.int64), prob_val=pf[nz].astype(np.float32), nnz=np.int64(nnz),
-                        logsumexp=torch.logsumexp(x, -1).numpy().astype(np.float32))
+    out = dict(vocab=np.int64(V), running=np.asarray(running, np.float64), temperature=np.float64(temperature),
+               top_p=np.float64(top_p), offs=offs, idx=idx, val=vals, prob_idx=nz.astype(np.int64),
+               prob_val=pf[nz].astype(np.float32), nnz=np.int64(nnz),
+               logsumexp=torch.logsumexp(x, -1).numpy().astype(np.float32))
+    if extra is None:
+        out.update(logits=logits.astype(np.float32), seen=np.packbits(seen, axis=1))
+    else:
+        out.update(extra)
+    np.savez_compressed(os.path.join(HERE, f"beam_{name}.npz"), **out)
     print(f"beam_{name}: B={B} V={V} kept={np.diff(offs).tolist()} nnz={nnz}")
 
 
-def main(path):
+def big_cases(rs):
+    """The full-size configurations, inputs regenerated from bench.py's generators."""
+    sys.path.insert(0, ROOT)
+    import bench
+    # A 16-row slice of config 4: Zipf(1.1) histories of 4096 ids, T 1.5, top-p 0.9.
+    d = bench.cfg4(seed=11, rows=16)
+    seen = seen_of(d["history"], V_BIG)
+    proc_case(rs, "cfg4z", d["logits"], seen, 1.5, 0.9, 1, store_inputs=False,
+              extra=dict(gen="cfg4", gen_seed=np.int64(11), gen_rows=np.int64(16),
+                         sha=digest(d["logits"], d["history"])))
+    # Config 3: 8 beams, bf16-valued N(0,3^2) logits with 1 % of ids +6, V=49152,
+    # histories of 8000 ids, running scores U(-200,-10).
+    d = bench.cfg3(seed=12)
+    beam_case(rs, "cfg3", d["logits"], seen_of(d["history"], V_BIG), d["running"],
+              extra=dict(gen="cfg3", gen_seed=np.int64(12), sha=digest(d["logits"], d["history"])))
+    print("beam_cfg3 written")
+    # Config 5: 256 rows of 16384 tokens, the first half ending in a window repeated 3 times.
+    t = bench.cfg5_tokens(seed=13)
+    verdict = np.array([rs._repeating(row.tolist()) for row in t], bool)
+    np.savez_compressed(os.path.join(HERE, "repeat_cfg5.npz"), verdict=verdict, gen="cfg5_tokens",
+                        gen_seed=np.int64(13), sha=digest(t))
+    print("repeat_cfg5:", int(verdict.sum()), "of", len(verdict), "repeating")
+
+
+def main(path, only=None):
     rs = load_reference(path)
+    if only == "big":
+        big_cases(rs)
+        return
     rng = np.random.default_rng(20261201)
 
     # The reference's own processor pin (tests/test_generation.py:109-122).
@@ -201,7 +249,15 @@ def main(path):
     verdict = np.array([rs._repeating(list(r)) for r in rows], bool)
     np.savez_compressed(os.path.join(HERE, "repeat.npz"), tokens=mat, lengths=lengths, verdict=verdict)
     print("repeat:", verdict.astype(int).tolist())
+    big_cases(rs)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("STARVECTOR_REF"),
+                    help="checkout of ComfyUI-StarVector-GGUF (or STARVECTOR_REF)")
+    ap.add_argument("--only", choices=["big"], default=None, help="write only the full-size fixtures")
+    args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set STARVECTOR_REF")
+    main(args.reference, args.only)

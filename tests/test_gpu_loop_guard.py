@@ -5,7 +5,7 @@ import pytest
 import torch
 
 import bench
-from _golden import GOLDEN
+from _golden import GOLDEN, cfg5_fixture
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -26,6 +26,13 @@ def test_cfg5_full_size_verdicts(sv):
     ref = O.repeating(t)
     np.testing.assert_array_equal(v.cpu().numpy(), ref)
     assert ref[:128].all() and not ref[128:].any()
+
+
+def test_cfg5_reference_verdicts(sv):
+    """Config 5 at full size against the reference's own _repeating verdicts."""
+    t, verdict = cfg5_fixture()
+    v = sv.loop_guard(torch.from_numpy(t).to(DEV))
+    np.testing.assert_array_equal(v.cpu().numpy(), verdict)
 
 
 @pytest.mark.parametrize("window,repeats", [(1, 3), (8, 2), (64, 3), (64, 5), (200, 3), (1024, 2)])
