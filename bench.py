@@ -517,15 +517,31 @@ def latency_extras(sv, dev):
     return out
 
 
-def vocab_sharded_extra(sv, dev, rank, world, steps=20, warmup=3):
+def _graph_time_ranks(fn, dev, steps):
+    """Device time per call of fn (a captured step's replay), max over ranks."""
+    import torch
+    import torch.distributed as dist
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) * 1e3 / steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0])
+
+
+def vocab_sharded_extra(sv, dev, rank, world, steps=20):
     """Config 5's vocab-sharded sample step: 256 rows, V split across the ranks
-    (slice step, one NCCL all-gather of the top-50 lists, merge on every rank).
-    Device time per step, max over ranks."""
+    (slice step into the exchange block, one NCCL all-gather, merge on every rank),
+    captured as one CUDA graph per rank.  Device time per step, max over ranks."""
     import torch
     import torch.distributed as dist
     rows, cap = 256, 64
-    w = V // world
-    off = rank * w
+    off, w, stride = sv.sharded.slice_bounds(V, rank, world)
     g = np.random.default_rng(5)  # the same rows on every rank
     x = (2.0 * g.standard_normal((rows, V))).astype(np.float32)
     ids = g.integers(0, V, (rows, 16384))
@@ -536,38 +552,29 @@ def vocab_sharded_extra(sv, dev, rank, world, steps=20, warmup=3):
     seen[np.arange(rows)[:, None], ids] = True
     packed = np.packbits(seen, axis=1, bitorder="little")  # V is a multiple of 32
     bits = torch.from_numpy(np.ascontiguousarray(packed).view(np.int32)).to(dev)
-    out = {}
-
-    def step():
-        sv.sharded.sample_step_vocab_sharded(xd, ud, offset=off, seen_bits=bits, capacity=cap, out=out)
-
-    for _ in range(warmup):
+    step = sv.sharded.VocabShardedSampler(xd, ud, offset=off, slice_stride=stride, seen_bits=bits,
+                                          capacity=cap).capture()
+    try:
         step()
-    torch.cuda.synchronize()
-    bad = int(out["status"].max().item())
-    dist.barrier()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([a.elapsed_time(b) * 1e3 / steps, float(bad)], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return {"cfg5_vocab_sharded_us_per_step": float(t[0]), "cfg5_vocab_sharded_slices": world,
-            "cfg5_vocab_sharded_max_status": int(t[1])}
+        torch.cuda.synchronize()
+        bad = torch.tensor([float(step.out["status"].max().item())], device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        us = _graph_time_ranks(step, dev, steps)
+    finally:
+        step.release()
+    return {"cfg5_vocab_sharded_us_per_step": us, "cfg5_vocab_sharded_slices": world,
+            "cfg5_vocab_sharded_max_status": int(bad.item()), "cfg5_vocab_sharded_graph": True}
 
 
-def vocab_sharded_beam_extra(sv, dev, rank, world, steps=20, warmup=3):
+def vocab_sharded_beam_extra(sv, dev, rank, world, steps=20):
     """Config 3's beam step with every beam's vocabulary split across the ranks
-    (slice statistics, two NCCL all-reduces, slice step, one all-gather, merge).
-    Device time per step, max over ranks."""
+    (slice statistics, two NCCL all-reduces, slice step, one all-gather, merge),
+    captured as one CUDA graph per rank.  Device time per step, max over ranks."""
     import torch
     import torch.distributed as dist
     d = cfg3()
     beams, cap = d["logits"].shape[0], 64
-    w = V // world
-    off = rank * w
+    off, w, stride = sv.sharded.slice_bounds(V, rank, world)
     xd = torch.from_numpy(np.ascontiguousarray(d["logits"][:, off:off + w])).to(dev).to(torch.bfloat16)
     seen = np.zeros((beams, V), bool)
     seen[np.arange(beams)[:, None], d["history"]] = True
@@ -575,25 +582,18 @@ def vocab_sharded_beam_extra(sv, dev, rank, world, steps=20, warmup=3):
     bits = torch.from_numpy(np.ascontiguousarray(packed).view(np.int32)).to(dev)
     rs = torch.from_numpy(d["running"]).to(dev)
     ud = torch.from_numpy(d["uniforms"]).to(dev)
-    out = {}
-
-    def step():
-        sv.sharded.beam_step_vocab_sharded(xd, rs, ud, offset=off, vocab=V, seen_bits=bits, capacity=cap, out=out)
-
-    for _ in range(warmup):
+    step = sv.sharded.VocabShardedBeamStep(xd, rs, ud, offset=off, vocab=V, slice_stride=stride, seen_bits=bits,
+                                           capacity=cap).capture()
+    try:
         step()
-    torch.cuda.synchronize()
-    bad = int(out["status"].max().item())
-    dist.barrier()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([a.elapsed_time(b) * 1e3 / steps, float(bad)], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return {"cfg3_vocab_sharded_beam_us_per_step": float(t[0]), "cfg3_vocab_sharded_beam_max_status": int(t[1])}
+        torch.cuda.synchronize()
+        bad = torch.tensor([float(step.out["status"].max().item())], device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        us = _graph_time_ranks(step, dev, steps)
+    finally:
+        step.release()
+    return {"cfg3_vocab_sharded_beam_us_per_step": us, "cfg3_vocab_sharded_beam_max_status": int(bad.item()),
+            "cfg3_vocab_sharded_beam_graph": True}
 
 
 def main():

@@ -39,6 +39,9 @@ _SIGNATURES = {
     "sv_merge_beam_shards_workspace_bytes": (_SZ, [_I32, _I32, _I32]),
     "sv_merge_beam_shards": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _D, _I32, _I32, _P, _SZ,
                                     _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P]),
+    "sv_merge_slices": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _D, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P]),
+    "sv_merge_beam_slices": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _D, _I32, _I32, _P, _SZ,
+                                    _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P]),
     "sv_error_string": (C.c_char_p, [_I32]),
     "sv_abi_version": (_I32, []),
 }

@@ -11,12 +11,20 @@
 // ascending (value, index) order with exact fixed-point mass (:182-186) and the
 // draw from the row's uniform (:201).
 //
-// Wire format (int32, one record per shard and row):
-//   [0, C)      warped scores (float bits), the slice's kept tokens in index order
-//   [C, 2C)     their global vocabulary indices
-//   2C          kept count of the slice (may exceed C: the list was truncated)
-//   2C + 1      the slice's status (SV_ST_*)
+// Wire formats (int32):
+//   records (sv_pack_slice, one record per shard and row):
+//     [0, C)      warped scores (float bits), the slice's kept tokens in index order
+//     [C, 2C)     their global vocabulary indices
+//     2C          kept count of the slice (may exceed C: the list was truncated)
+//     2C + 1      the slice's status (SV_ST_*)
+//   blocks (one per shard, written directly by the slice's sv_sample_step):
+//     [0, RC)          warped scores (float bits) [rows][C]
+//     [RC, 2RC)        slice-local indices [rows][C] (shard s adds s * slice_stride)
+//     [2RC, 2RC + R)   kept counts
+//     [2RC + R, 2RC + 2R) statuses
 #include <cuda_runtime.h>
+
+#include <cstdint>
 
 #include "../../include/starvector_sampling.h"
 #include "sv_block.cuh"
@@ -48,6 +56,9 @@ struct MergeArgs {
   unsigned char* ws;
   int ws_cap;
   float* out_score;
+  // Blocked input (blocked != 0): shard s's block at packed + s * (2 rows cap +
+  // 2 rows), its indices offset by s * slice_stride.
+  int blocked, slice_stride;
 };
 
 struct __align__(16) MergeShared {
@@ -74,8 +85,22 @@ __global__ void __launch_bounds__(MNT) merge_kernel(const MergeArgs m, const Row
   // Union of the shards' lists.  A shard without a finite score contributes
   // nothing; any other shard error is the row's.
   for (int s = 0; s < m.shards; ++s) {
-    const int32_t* r = m.packed + ((int64_t)s * m.rows + row) * rec;
-    const int cnt = r[2 * m.cap], st = r[2 * m.cap + 1];
+    const int32_t* r;  // the row's scores; its indices follow at ids
+    const int32_t* ids;
+    int cnt, st, off = 0;
+    if (m.blocked) {
+      const int32_t* blk = m.packed + (int64_t)s * (2 * (int64_t)m.rows * m.cap + 2 * m.rows);
+      r = blk + (int64_t)row * m.cap;
+      ids = blk + (int64_t)m.rows * m.cap + (int64_t)row * m.cap;
+      cnt = blk[2 * (int64_t)m.rows * m.cap + row];
+      st = blk[2 * (int64_t)m.rows * m.cap + m.rows + row];
+      off = s * m.slice_stride;
+    } else {
+      r = m.packed + ((int64_t)s * m.rows + row) * rec;
+      ids = r + m.cap;
+      cnt = r[2 * m.cap];
+      st = r[2 * m.cap + 1];
+    }
     if (st == ST_ALLNEGINF) continue;
     if (st != ST_OK) {
       if (tid == 0) sh.err |= 1 << st;
@@ -87,7 +112,7 @@ __global__ void __launch_bounds__(MNT) merge_kernel(const MergeArgs m, const Row
     const int base = sh.n;
     for (int j = tid; j < take; j += MNT) {
       sh.cv[base + j] = __int_as_float(r[j]);
-      sh.ci[base + j] = r[m.cap + j];
+      sh.ci[base + j] = ids[j] + off;
     }
     __syncthreads();
     if (tid == 0) sh.n = base + take;
@@ -240,16 +265,17 @@ extern "C" int sv_pack_slice(const int32_t* count, const int32_t* status, const 
   return cudaGetLastError() == cudaSuccess ? SV_OK : SV_E_CUDA;
 }
 
-// Merges the all-gathered per-shard kept lists of a vocab-sharded sample step; see
-// include/starvector_sampling.h.
-extern "C" int sv_merge_shards(const int32_t* packed, int32_t shards, int32_t rows, int32_t capacity,
-                               const float* uniforms, double top_p, int32_t top_k, int32_t keep,
-                               int64_t* out_token, int32_t* out_count, int32_t* out_idx, float* out_prob,
-                               int32_t out_capacity, int32_t* out_status, void* stream) {
+namespace {
+
+int merge_sample(const int32_t* packed, int blocked, int32_t slice_stride, int32_t shards, int32_t rows,
+                 int32_t capacity, const float* uniforms, double top_p, int32_t top_k, int32_t keep,
+                 int64_t* out_token, int32_t* out_count, int32_t* out_idx, float* out_prob, int32_t out_capacity,
+                 int32_t* out_status, void* stream) {
   if (!packed || !uniforms || !out_token) return SV_E_ARG;
   if (out_capacity > 0 && !out_idx && !out_prob) return SV_E_ARG;
   if (shards < 1 || rows < 1 || capacity < 1 || (int64_t)shards * capacity > kMergeMax || out_capacity < 0)
     return SV_E_SHAPE;
+  if (blocked && (slice_stride < 1 || (int64_t)(shards - 1) * slice_stride > INT32_MAX)) return SV_E_SHAPE;
   if (!(top_p > 0.0 && top_p <= 1.0)) return SV_E_RANGE;
   if (top_k < 1 || top_k > kMaxTopK || keep < 1 || keep > kMaxTopK) return SV_E_RANGE;
   const int kk = top_k > keep ? top_k : keep;
@@ -260,8 +286,31 @@ extern "C" int sv_merge_shards(const int32_t* packed, int32_t shards, int32_t ro
   a.pthr = top_p < 1.0 ? (float)(1.0 - top_p) : 0.0f;
   MergeArgs m = {packed, shards, rows, capacity, uniforms, out_token, out_count, out_idx, out_prob, out_capacity,
                  out_status};
+  m.blocked = blocked;
+  m.slice_stride = slice_stride;
   merge_kernel<<<rows, MNT, 0, static_cast<cudaStream_t>(stream)>>>(m, a);
   return cudaGetLastError() == cudaSuccess ? SV_OK : SV_E_CUDA;
+}
+
+}  // namespace
+
+// Merges the all-gathered per-shard kept lists of a vocab-sharded sample step; see
+// include/starvector_sampling.h.
+extern "C" int sv_merge_shards(const int32_t* packed, int32_t shards, int32_t rows, int32_t capacity,
+                               const float* uniforms, double top_p, int32_t top_k, int32_t keep,
+                               int64_t* out_token, int32_t* out_count, int32_t* out_idx, float* out_prob,
+                               int32_t out_capacity, int32_t* out_status, void* stream) {
+  return merge_sample(packed, 0, 0, shards, rows, capacity, uniforms, top_p, top_k, keep, out_token, out_count,
+                      out_idx, out_prob, out_capacity, out_status, stream);
+}
+
+// The same merge over the all-gathered slice blocks; see include/starvector_sampling.h.
+extern "C" int sv_merge_slices(const int32_t* blocks, int32_t shards, int32_t rows, int32_t capacity,
+                               int32_t slice_stride, const float* uniforms, double top_p, int32_t top_k,
+                               int32_t keep, int64_t* out_token, int32_t* out_count, int32_t* out_idx,
+                               float* out_prob, int32_t out_capacity, int32_t* out_status, void* stream) {
+  return merge_sample(blocks, 1, slice_stride, shards, rows, capacity, uniforms, top_p, top_k, keep, out_token,
+                      out_count, out_idx, out_prob, out_capacity, out_status, stream);
 }
 
 // ------------------------------------------------- vocab-sharded beam step (C ABI)
@@ -342,15 +391,14 @@ extern "C" size_t sv_merge_beam_shards_workspace_bytes(int32_t beams, int32_t sh
   return sizeof(BeamWsHeader) + (size_t)beams * (size_t)shards * (size_t)capacity * 16;
 }
 
-// Merge side of the vocab-sharded beam step; see include/starvector_sampling.h.
-extern "C" int sv_merge_beam_shards(const int32_t* packed, int32_t shards, int32_t beams, int32_t capacity,
-                                    int32_t vocab, const float* global_max, const int32_t* global_flags,
-                                    const float* running_scores, const float* uniforms, int32_t num_picks,
-                                    double top_p, int32_t top_k, int32_t keep, void* workspace,
-                                    size_t workspace_bytes, int64_t* out_picks, float* out_pick_scores,
-                                    int32_t* out_num_picks, int32_t* out_status, int32_t* out_kept_count,
-                                    int32_t* out_kept_idx, float* out_kept_logprob, float* out_kept_prob,
-                                    int32_t out_capacity, void* stream) {
+namespace {
+
+int merge_beam(const int32_t* packed, int blocked, int32_t slice_stride, int32_t shards, int32_t beams,
+               int32_t capacity, int32_t vocab, const float* global_max, const int32_t* global_flags,
+               const float* running_scores, const float* uniforms, int32_t num_picks, double top_p, int32_t top_k,
+               int32_t keep, void* workspace, size_t workspace_bytes, int64_t* out_picks, float* out_pick_scores,
+               int32_t* out_num_picks, int32_t* out_status, int32_t* out_kept_count, int32_t* out_kept_idx,
+               float* out_kept_logprob, float* out_kept_prob, int32_t out_capacity, void* stream) {
   if (!packed || !global_max || !global_flags || !running_scores || !uniforms || !workspace || !out_picks ||
       !out_pick_scores || !out_num_picks || !out_status)
     return SV_E_ARG;
@@ -358,6 +406,7 @@ extern "C" int sv_merge_beam_shards(const int32_t* packed, int32_t shards, int32
   if (shards < 1 || beams < 1 || beams > kMaxBeams || capacity < 1 || (int64_t)shards * capacity > kMergeMax ||
       vocab < 1 || out_capacity < 0)
     return SV_E_SHAPE;
+  if (blocked && (slice_stride < 1 || (int64_t)(shards - 1) * slice_stride >= vocab)) return SV_E_SHAPE;
   if (num_picks < 1 || num_picks > 64) return SV_E_RANGE;
   if (!(top_p > 0.0 && top_p <= 1.0)) return SV_E_RANGE;
   if (top_k < 1 || top_k > kMaxTopK || keep < 1 || keep > kMaxTopK) return SV_E_RANGE;
@@ -373,6 +422,8 @@ extern "C" int sv_merge_beam_shards(const int32_t* packed, int32_t shards, int32
   MergeArgs m = {packed, shards, beams, capacity, uniforms, nullptr, out_kept_count, out_kept_idx, nullptr,
                  out_capacity, nullptr, global_max, global_flags, static_cast<unsigned char*>(workspace),
                  shards * capacity, out_kept_logprob};
+  m.blocked = blocked;
+  m.slice_stride = slice_stride;
   merge_kernel<<<beams, MNT, 0, s>>>(m, a);
   if (cudaGetLastError() != cudaSuccess) return SV_E_CUDA;
   RowArgs b = {};
@@ -391,4 +442,36 @@ extern "C" int sv_merge_beam_shards(const int32_t* packed, int32_t shards, int32
   b.out_prob = out_kept_prob;
   b.out_cap = out_capacity;
   return launch_beam_merge(b, s) == cudaSuccess ? SV_OK : SV_E_CUDA;
+}
+
+}  // namespace
+
+// Merge side of the vocab-sharded beam step; see include/starvector_sampling.h.
+extern "C" int sv_merge_beam_shards(const int32_t* packed, int32_t shards, int32_t beams, int32_t capacity,
+                                    int32_t vocab, const float* global_max, const int32_t* global_flags,
+                                    const float* running_scores, const float* uniforms, int32_t num_picks,
+                                    double top_p, int32_t top_k, int32_t keep, void* workspace,
+                                    size_t workspace_bytes, int64_t* out_picks, float* out_pick_scores,
+                                    int32_t* out_num_picks, int32_t* out_status, int32_t* out_kept_count,
+                                    int32_t* out_kept_idx, float* out_kept_logprob, float* out_kept_prob,
+                                    int32_t out_capacity, void* stream) {
+  return merge_beam(packed, 0, 0, shards, beams, capacity, vocab, global_max, global_flags, running_scores, uniforms,
+                    num_picks, top_p, top_k, keep, workspace, workspace_bytes, out_picks, out_pick_scores,
+                    out_num_picks, out_status, out_kept_count, out_kept_idx, out_kept_logprob, out_kept_prob,
+                    out_capacity, stream);
+}
+
+// The same over the all-gathered slice blocks; see include/starvector_sampling.h.
+extern "C" int sv_merge_beam_slices(const int32_t* blocks, int32_t shards, int32_t beams, int32_t capacity,
+                                    int32_t slice_stride, int32_t vocab, const float* global_max,
+                                    const int32_t* global_flags, const float* running_scores, const float* uniforms,
+                                    int32_t num_picks, double top_p, int32_t top_k, int32_t keep, void* workspace,
+                                    size_t workspace_bytes, int64_t* out_picks, float* out_pick_scores,
+                                    int32_t* out_num_picks, int32_t* out_status, int32_t* out_kept_count,
+                                    int32_t* out_kept_idx, float* out_kept_logprob, float* out_kept_prob,
+                                    int32_t out_capacity, void* stream) {
+  return merge_beam(blocks, 1, slice_stride, shards, beams, capacity, vocab, global_max, global_flags, running_scores,
+                    uniforms, num_picks, top_p, top_k, keep, workspace, workspace_bytes, out_picks, out_pick_scores,
+                    out_num_picks, out_status, out_kept_count, out_kept_idx, out_kept_logprob, out_kept_prob,
+                    out_capacity, stream);
 }

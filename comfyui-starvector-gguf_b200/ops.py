@@ -246,19 +246,46 @@ def seen_reorder(src, dst, parents, tokens, vocab):
     L.check(rc, "sv_seen_reorder")
 
 
-def merge_shards(packed, uniforms, *, capacity, top_p=0.9, top_k=50, keep=1, out_capacity=0, out=None):
-    """Merges the all-gathered per-slice kept lists of a vocab-sharded sample step
-    (sv_merge_shards): packed int32 [shards, rows, 2 * capacity + 2].
+def block_len(rows, capacity):
+    """int32 values of one rank's slice block (the sv_merge_slices layout)."""
+    return 2 * rows * capacity + 2 * rows
+
+
+def slice_block_outputs(block, rows, capacity):
+    """sample_step's `out` dict over one slice block int32 [block_len]: the slice
+    step writes its scores, slice-local ids, counts and statuses straight into the
+    exchange layout (the token goes to a separate int64 [rows])."""
+    RC = rows * capacity
+    return {"score": block[:RC].view(torch.float32).view(rows, capacity),
+            "idx": block[RC:2 * RC].view(rows, capacity),
+            "count": block[2 * RC:2 * RC + rows],
+            "status": block[2 * RC + rows:2 * RC + 2 * rows],
+            "token": torch.empty(rows, dtype=torch.int64, device=block.device)}
+
+
+def merge_shards(packed, uniforms, *, capacity, top_p=0.9, top_k=50, keep=1, out_capacity=0, out=None,
+                 rows=None, slice_stride=None):
+    """Merges the all-gathered per-slice kept lists of a vocab-sharded sample step:
+    records int32 [shards, rows, 2 * capacity + 2] (sv_merge_shards), or with
+    slice_stride given, slice blocks int32 [shards, block_len(rows, capacity)]
+    (sv_merge_slices).
 
     Returns a dict: token int64 [rows], count int32 [rows], status int32 [rows],
     and idx / prob [rows, out_capacity] when out_capacity > 0.
     """
     _need_cuda(packed, "packed")
-    if packed.dtype != torch.int32 or packed.dim() != 3 or not packed.is_contiguous():
-        raise ValueError("packed must be a contiguous int32 tensor [shards, rows, 2 * capacity + 2]")
-    S, R, W = packed.shape
-    if W != 2 * capacity + 2:
-        raise ValueError("packed records must hold 2 * capacity + 2 values")
+    blocked = slice_stride is not None
+    if blocked:
+        if packed.dtype != torch.int32 or packed.dim() != 2 or not packed.is_contiguous() or rows is None or \
+                packed.shape[1] != block_len(rows, capacity):
+            raise ValueError("blocks must be a contiguous int32 tensor [shards, 2 rows capacity + 2 rows]")
+        S, R = packed.shape[0], int(rows)
+    else:
+        if packed.dtype != torch.int32 or packed.dim() != 3 or not packed.is_contiguous():
+            raise ValueError("packed must be a contiguous int32 tensor [shards, rows, 2 * capacity + 2]")
+        S, R, W = packed.shape
+        if W != 2 * capacity + 2:
+            raise ValueError("packed records must hold 2 * capacity + 2 values")
     u = uniforms.reshape(-1)
     _need_cuda(u, "uniforms")
     if u.dtype != torch.float32 or not u.is_contiguous() or u.numel() < R:
@@ -274,10 +301,17 @@ def merge_shards(packed, uniforms, *, capacity, top_p=0.9, top_k=50, keep=1, out
     for k, make in need.items():
         if k not in o:
             o[k] = make()
-    rc = L.lib().sv_merge_shards(packed.data_ptr(), S, R, int(capacity), u.data_ptr(), float(top_p), int(top_k),
-                                 int(keep), o["token"].data_ptr(), o["count"].data_ptr(), _ptr(o.get("idx")),
-                                 _ptr(o.get("prob")), int(out_capacity), o["status"].data_ptr(), _stream(dev))
-    L.check(rc, "sv_merge_shards")
+    if blocked:
+        rc = L.lib().sv_merge_slices(packed.data_ptr(), S, R, int(capacity), int(slice_stride), u.data_ptr(),
+                                     float(top_p), int(top_k), int(keep), o["token"].data_ptr(),
+                                     o["count"].data_ptr(), _ptr(o.get("idx")), _ptr(o.get("prob")),
+                                     int(out_capacity), o["status"].data_ptr(), _stream(dev))
+        L.check(rc, "sv_merge_slices")
+    else:
+        rc = L.lib().sv_merge_shards(packed.data_ptr(), S, R, int(capacity), u.data_ptr(), float(top_p), int(top_k),
+                                     int(keep), o["token"].data_ptr(), o["count"].data_ptr(), _ptr(o.get("idx")),
+                                     _ptr(o.get("prob")), int(out_capacity), o["status"].data_ptr(), _stream(dev))
+        L.check(rc, "sv_merge_shards")
     return o
 
 
@@ -296,19 +330,22 @@ def pack_slice(local, offset, capacity, out):
     return out
 
 
-def beam_slice_stats(logits_slice, global_max=None):
+def beam_slice_stats(logits_slice, global_max=None, out=None):
     """One rank's slice statistics for the vocab-sharded beam step
     (sv_beam_slice_stats).  Without global_max: {"max": float [beams], "flags":
     int32 [beams]} (2 NaN, 1 +inf, 0 neither), to all-reduce with MAX.  With the
     reduced maxima: {"sum": int64 [beams]}, the exact fixed-point exp sums, to
-    all-reduce with SUM."""
+    all-reduce with SUM.  `out` may hold those tensors already (filled in place)."""
     x = _rows(logits_slice)
     B, W = x.shape
     dev = x.device
     stride = x.stride(0) if B > 1 else 0
+    o = out if out is not None else {}
     if global_max is None:
-        mx = torch.empty(B, dtype=torch.float32, device=dev)
-        fl = torch.empty(B, dtype=torch.int32, device=dev)
+        mx = o.get("max")
+        mx = mx if mx is not None else torch.empty(B, dtype=torch.float32, device=dev)
+        fl = o.get("flags")
+        fl = fl if fl is not None else torch.empty(B, dtype=torch.int32, device=dev)
         rc = L.lib().sv_beam_slice_stats(x.data_ptr(), _DTYPES[x.dtype], B, W, stride, None, mx.data_ptr(),
                                          fl.data_ptr(), None, _stream(dev))
         L.check(rc, "sv_beam_slice_stats")
@@ -317,7 +354,8 @@ def beam_slice_stats(logits_slice, global_max=None):
     _need_cuda(gm, "global_max")
     if gm.dtype != torch.float32 or not gm.is_contiguous() or gm.numel() != B:
         raise ValueError("global_max must be a contiguous float32 tensor [beams]")
-    sm = torch.empty(B, dtype=torch.int64, device=dev)
+    sm = o.get("sum")
+    sm = sm if sm is not None else torch.empty(B, dtype=torch.int64, device=dev)
     rc = L.lib().sv_beam_slice_stats(x.data_ptr(), _DTYPES[x.dtype], B, W, stride, gm.data_ptr(), None, None,
                                      sm.data_ptr(), _stream(dev))
     L.check(rc, "sv_beam_slice_stats")
@@ -344,16 +382,26 @@ def beam_slice_logprobs(logits_slice, global_max, global_sum, out=None):
 
 
 def merge_beam_shards(packed, global_max, global_flags, running_scores, uniforms, *, capacity, vocab, top_p=0.9,
-                      top_k=50, keep=2, num_picks=None, out_capacity=0, workspace=None, out=None):
-    """Merge side of the vocab-sharded beam step (sv_merge_beam_shards): packed int32
-    [shards, beams, 2 * capacity + 2].  Returns beam_step's dict (picks, scores, n,
-    status, and the per-beam kept lists when out_capacity > 0)."""
+                      top_k=50, keep=2, num_picks=None, out_capacity=0, workspace=None, out=None, beams=None,
+                      slice_stride=None):
+    """Merge side of the vocab-sharded beam step: records int32 [shards, beams,
+    2 * capacity + 2] (sv_merge_beam_shards), or with slice_stride given, slice
+    blocks int32 [shards, block_len(beams, capacity)] (sv_merge_beam_slices).
+    Returns beam_step's dict (picks, scores, n, status, and the per-beam kept lists
+    when out_capacity > 0)."""
     _need_cuda(packed, "packed")
-    if packed.dtype != torch.int32 or packed.dim() != 3 or not packed.is_contiguous():
-        raise ValueError("packed must be a contiguous int32 tensor [shards, beams, 2 * capacity + 2]")
-    S, B, Wd = packed.shape
-    if Wd != 2 * capacity + 2:
-        raise ValueError("packed records must hold 2 * capacity + 2 values")
+    blocked = slice_stride is not None
+    if blocked:
+        if packed.dtype != torch.int32 or packed.dim() != 2 or not packed.is_contiguous() or beams is None or \
+                packed.shape[1] != block_len(beams, capacity):
+            raise ValueError("blocks must be a contiguous int32 tensor [shards, 2 beams capacity + 2 beams]")
+        S, B = packed.shape[0], int(beams)
+    else:
+        if packed.dtype != torch.int32 or packed.dim() != 3 or not packed.is_contiguous():
+            raise ValueError("packed must be a contiguous int32 tensor [shards, beams, 2 * capacity + 2]")
+        S, B, Wd = packed.shape
+        if Wd != 2 * capacity + 2:
+            raise ValueError("packed records must hold 2 * capacity + 2 values")
     P = 2 * B if num_picks is None else int(num_picks)
     dev = packed.device
     rs, u = running_scores.reshape(-1), uniforms.reshape(-1)
@@ -384,11 +432,15 @@ def merge_beam_shards(packed, global_max, global_flags, running_scores, uniforms
         if ws is None:
             nbytes = L.lib().sv_merge_beam_shards_workspace_bytes(B, S, int(capacity))
             ws = _WORKSPACES[key] = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    rc = L.lib().sv_merge_beam_shards(
-        packed.data_ptr(), S, B, int(capacity), int(vocab), gm.data_ptr(), gf.data_ptr(), rs.data_ptr(),
-        u.data_ptr(), P, float(top_p), int(top_k), int(keep), ws.data_ptr(), ws.numel(), o["picks"].data_ptr(),
-        o["scores"].data_ptr(), o["n"].data_ptr(), o["status"].data_ptr(), _ptr(o.get("kept_count")),
-        _ptr(o.get("kept_idx")), _ptr(o.get("kept_logprob")), _ptr(o.get("kept_prob")), int(out_capacity),
-        _stream(dev))
-    L.check(rc, "sv_merge_beam_shards")
+    tail = (gm.data_ptr(), gf.data_ptr(), rs.data_ptr(), u.data_ptr(), P, float(top_p), int(top_k), int(keep),
+            ws.data_ptr(), ws.numel(), o["picks"].data_ptr(), o["scores"].data_ptr(), o["n"].data_ptr(),
+            o["status"].data_ptr(), _ptr(o.get("kept_count")), _ptr(o.get("kept_idx")), _ptr(o.get("kept_logprob")),
+            _ptr(o.get("kept_prob")), int(out_capacity), _stream(dev))
+    if blocked:
+        rc = L.lib().sv_merge_beam_slices(packed.data_ptr(), S, B, int(capacity), int(slice_stride), int(vocab),
+                                          *tail)
+        L.check(rc, "sv_merge_beam_slices")
+    else:
+        rc = L.lib().sv_merge_beam_shards(packed.data_ptr(), S, B, int(capacity), int(vocab), *tail)
+        L.check(rc, "sv_merge_beam_shards")
     return o

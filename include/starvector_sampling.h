@@ -260,6 +260,31 @@ int sv_merge_beam_shards(const int32_t* packed, int32_t shards, int32_t beams, i
                          int32_t* out_num_picks, int32_t* out_status, int32_t* out_kept_count, int32_t* out_kept_idx,
                          float* out_kept_logprob, float* out_kept_prob, int32_t out_capacity, void* stream);
 
+/*
+ * The same merges over slice blocks, the exchange layout a rank's sv_sample_step
+ * (or its beam slice step) writes directly, so no packing launch is needed.  No
+ * counterpart in the reference (it has no sharded vocabulary).  Each shard's block
+ * is int32 [2 * rows * capacity + 2 * rows]:
+ *   [0, rows * capacity)                    out_score [rows][capacity] (float bits)
+ *   [rows * capacity, 2 * rows * capacity)  out_idx [rows][capacity], slice-local
+ *   [2 * rows * capacity, + rows)           out_count [rows]
+ *   [2 * rows * capacity + rows, + rows)    out_status [rows]
+ * and `blocks` holds the shards' blocks back to back (an all-gather of each rank's
+ * block).  Shard s's indices are offset by s * slice_stride (its slice starts
+ * there).  Otherwise as sv_merge_shards / sv_merge_beam_shards.
+ */
+int sv_merge_slices(const int32_t* blocks, int32_t shards, int32_t rows, int32_t capacity, int32_t slice_stride,
+                    const float* uniforms, double top_p, int32_t top_k, int32_t keep, int64_t* out_token,
+                    int32_t* out_count, int32_t* out_idx, float* out_prob, int32_t out_capacity, int32_t* out_status,
+                    void* stream);
+int sv_merge_beam_slices(const int32_t* blocks, int32_t shards, int32_t beams, int32_t capacity, int32_t slice_stride,
+                         int32_t vocab, const float* global_max, const int32_t* global_flags,
+                         const float* running_scores, const float* uniforms, int32_t num_picks, double top_p,
+                         int32_t top_k, int32_t keep, void* workspace, size_t workspace_bytes, int64_t* out_picks,
+                         float* out_pick_scores, int32_t* out_num_picks, int32_t* out_status,
+                         int32_t* out_kept_count, int32_t* out_kept_idx, float* out_kept_logprob,
+                         float* out_kept_prob, int32_t out_capacity, void* stream);
+
 /* Text of a return or status code. */
 const char* sv_error_string(int32_t code);
 

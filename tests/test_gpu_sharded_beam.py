@@ -4,8 +4,9 @@ Each slice runs the rank-side calls of sharded.beam_step_vocab_sharded:
 - its statistics (sv_beam_slice_stats), reduced across the slices as the all-reduces
   would (MAX of maxima and flags, SUM of the int64 exp sums);
 - its log_softmax (sv_beam_slice_logprobs) and slice step;
-- its exchange records, stacked as an all-gather lays them out, then
-  sv_merge_beam_shards.
+- its exchange block written by the slice step (sv_merge_beam_slices' layout)
+  or packed records (sv_pack_slice, for sv_merge_beam_shards), stacked as an
+  all-gather lays them out, then the merge.
 
 Picks, picked scores, pick count, status and the per-beam kept lists must equal the
 oracle's beam step on the whole rows, bit for bit.
@@ -26,7 +27,8 @@ def bitmap(seen):
     return torch.from_numpy(np.ascontiguousarray(b).view(np.int32)).to(DEV)
 
 
-def run_sharded(sv, x, seen, running, u, shards, cap, dtype=torch.float32, T=1.5, p=0.9, top_k=50, out_cap=128):
+def run_sharded(sv, x, seen, running, u, shards, cap, dtype=torch.float32, T=1.5, p=0.9, top_k=50, out_cap=128,
+                layout="blocks"):
     B, V = x.shape
     xd = torch.from_numpy(x).to(DEV).to(dtype)
     rs = torch.from_numpy(running).to(DEV)
@@ -38,16 +40,23 @@ def run_sharded(sv, x, seen, running, u, shards, cap, dtype=torch.float32, T=1.5
     gmax = torch.stack([f["max"] for f in first]).amax(0).contiguous()
     gflags = torch.stack([f["flags"] for f in first]).amax(0).contiguous()
     gsum = torch.stack([sv.ops.beam_slice_stats(t, global_max=gmax)["sum"] for t in sl]).sum(0).contiguous()
-    recs = []
+    parts = []
     dummy = torch.zeros(B, dtype=torch.float32, device=DEV)
     for s, t in enumerate(sl):
         lp = sv.ops.beam_slice_logprobs(t, gmax, gsum)
-        loc = sv.sharded.slice_step(lp, dummy, offset=s * w, seen_bits=bits, temperature=T, top_k=top_k, keep=2,
-                                    capacity=cap)
-        recs.append(sv.sharded.pack_slice(loc, s * w, cap))
-    packed = torch.stack(recs).contiguous()
+        kw = dict(offset=s * w, seen_bits=bits, temperature=T, top_k=top_k, keep=2, capacity=cap)
+        if layout == "blocks":
+            blk = torch.empty(sv.ops.block_len(B, cap), dtype=torch.int32, device=DEV)
+            sv.sharded.slice_step(lp, dummy, out=sv.ops.slice_block_outputs(blk, B, cap), **kw)
+            parts.append(blk)
+        else:
+            loc = sv.sharded.slice_step(lp, dummy, **kw)
+            rec = torch.empty((B, 2 * cap + 2), dtype=torch.int32, device=DEV)
+            parts.append(sv.ops.pack_slice(loc, s * w, cap, rec))
+    packed = torch.stack(parts).contiguous()
+    extra = dict(beams=B, slice_stride=w) if layout == "blocks" else {}
     out = sv.ops.merge_beam_shards(packed, gmax, gflags, rs, ud, capacity=cap, vocab=V, top_p=p, top_k=top_k,
-                                   keep=2, out_capacity=out_cap)
+                                   keep=2, out_capacity=out_cap, **extra)
     torch.cuda.synchronize()
     return {k: v.cpu().numpy() for k, v in out.items()}, xd.float().cpu().numpy()
 
@@ -76,9 +85,10 @@ def oracle_beam(xf, seen, running, u, T=1.5, p=0.9, top_k=50):
     return O.beam(xf, running, u, seen=seen, temperature=T, top_p=p, top_k=top_k, keep=2, npick=len(u))
 
 
+@pytest.mark.parametrize("layout", ["blocks", "records"])
 @pytest.mark.parametrize("beams,dtype,shards", [(2, torch.float32, 8), (8, torch.bfloat16, 8), (3, torch.float16, 4),
                                                 (1, torch.float32, 2)])
-def test_slices_match_whole_rows(sv, beams, dtype, shards):
+def test_slices_match_whole_rows(sv, beams, dtype, shards, layout):
     """Config 2 / 3 shapes (V = 49152) split into slices of 6144 or more."""
     g = np.random.default_rng(40 + beams)
     x = (2.5 * g.standard_normal((beams, 49152))).astype(np.float32)
@@ -87,7 +97,7 @@ def test_slices_match_whole_rows(sv, beams, dtype, shards):
     np.put_along_axis(seen, g.integers(0, 49152, (beams, 3000)), 1, axis=1)
     running = np.sort(g.uniform(-60, 0, beams)).astype(np.float32)[::-1].copy()
     u = g.random(2 * beams).astype(np.float32)
-    got, xf = run_sharded(sv, x, seen, running, u, shards, cap=64, dtype=dtype)
+    got, xf = run_sharded(sv, x, seen, running, u, shards, cap=64, dtype=dtype, layout=layout)
     check(got, oracle_beam(xf, seen, running, u))
 
 

@@ -1,7 +1,7 @@
 """Host side of the multi-GPU paths, on CPU ranks (gloo, world size 2).
 
 The vocab-sharded step runs its real host pipeline (slicing of the logits and the
-seen mask, the exchange records, the all-gather, the merge's input layout) with
+seen mask, the exchange blocks, the all-gather, the merge's input layout) with
 the CUDA kernels replaced by the oracle: the per-slice step is oracle.sample on the
 slice with top_p = 1, and the merge is oracle.sample, with temperature 1 and no
 penalty, on a row that holds only the gathered candidates (their warped scores at
@@ -49,8 +49,22 @@ def oracle_step(shard_logits, uniforms, *, offset, seen_bits=None, seen=None, te
             "score": torch.from_numpy(np.ascontiguousarray(score, np.float32))}
 
 
-def oracle_merge(packed, uniforms, *, capacity, top_p, top_k, keep, out_capacity, out=None):
-    p = packed.numpy()
+def records(blocks, rows, capacity, slice_stride):
+    """The all-gathered exchange blocks [shards, block_len] as per-shard records
+    [shards, rows, 2 * capacity + 2] with global ids (the layout the merge reads)."""
+    b = blocks.numpy()
+    S, RC = b.shape[0], rows * capacity
+    out = np.zeros((S, rows, 2 * capacity + 2), np.int32)
+    for s in range(S):
+        out[s, :, :capacity] = b[s, :RC].reshape(rows, capacity)
+        out[s, :, capacity:2 * capacity] = b[s, RC:2 * RC].reshape(rows, capacity) + s * slice_stride
+        out[s, :, 2 * capacity] = b[s, 2 * RC:2 * RC + rows]
+        out[s, :, 2 * capacity + 1] = b[s, 2 * RC + rows:]
+    return out
+
+
+def oracle_merge(blocks, uniforms, *, capacity, top_p, top_k, keep, out_capacity, out=None, rows, slice_stride):
+    p = records(blocks, rows, capacity, slice_stride)
     S, Rr, _ = p.shape
     sparse = np.full((Rr, V), -np.inf, np.float32)
     bad = np.zeros(Rr, np.int32)
@@ -175,12 +189,12 @@ def oracle_logprobs(shard_logits, gmax, gsum):
     return torch.from_numpy(((x - M[:, None]).astype(np.float32) - L[:, None]).astype(np.float32))
 
 
-def oracle_beam_merge(packed, gmax, gflags, running, uniforms, *, capacity, vocab, top_p, top_k, keep, num_picks,
-                      out_capacity, out=None):
+def oracle_beam_merge(blocks, gmax, gflags, running, uniforms, *, capacity, vocab, top_p, top_k, keep, num_picks,
+                      out_capacity, out=None, beams, slice_stride):
     """sv_merge_beam_shards restated on the host: each beam's kept list from the
     union (oracle.sample, temperature 1, on a row holding only the gathered warped
     log-probs), then the flattened softmax and the draws as oracle.beam makes them."""
-    p = packed.numpy()
+    p = records(blocks, beams, capacity, slice_stride)
     S, B, _ = p.shape
     fl, M, rs, u = gflags.numpy(), gmax.numpy(), running.numpy(), uniforms.numpy()
     sparse = np.full((B, vocab), -np.inf, np.float32)
