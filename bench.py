@@ -433,6 +433,8 @@ def run_ours(args, rank, world, local_rank):
     d2h = ROWS * 8
 
     extras = latency_extras(sv, dev) if rank == 0 and not args.no_extras else {}
+    if rank == 0 and not args.no_extras:
+        extras.update(kv_extras(sv, dev))
     if world > 1 and not args.no_extras:
         extras.update(vocab_sharded_extra(sv, dev, rank, world))  # every rank takes part
         extras.update(vocab_sharded_beam_extra(sv, dev, rank, world))
@@ -508,12 +510,42 @@ def latency_extras(sv, dev):
         ws = sv.beam_workspace(x.shape[0], x.shape[1], dev)
         sv.beam_step(x, rs, u, history=h, out=ob, workspace=ws)
         out[name] = graph_time_us(lambda: sv.beam_step(x, rs, u, history=h, out=ob, workspace=ws))
+    # Config 5's sampling rows (256 x V, 16384-token histories as a seen bitmap), on
+    # one GPU: the unsharded reference point of the vocab-sharded step.
+    xs, us_, bits = cfg5_sample_rows(dev)
+    o5 = {}
+    sv.sample_step(xs, us_, seen_bits=bits, out=o5)
+    out["cfg5_sample_unsharded_us_per_step"] = graph_time_us(lambda: sv.sample_step(xs, us_, seen_bits=bits, out=o5))
     t = torch.from_numpy(cfg5_tokens()).to(dev)
     lens = torch.full((t.shape[0],), t.shape[1], dtype=torch.int32, device=dev)
     v = torch.empty(t.shape[0], dtype=torch.uint8, device=dev)
     sv.loop_guard(t, lens, out=v)
     out["cfg5_loop_guard_us"] = graph_time_us(lambda: sv.loop_guard(t, lens, out=v))
     out["cfg5_loop_guard_GBps"] = t.numel() * 4 / (out["cfg5_loop_guard_us"] * 1e-6) / 1e9
+    return out
+
+
+def kv_extras(sv, dev):
+    """The beam KV-cache reorder (runtime_shared.py:388-394) on decoder-sized caches:
+    GPTBigCode-1B-like MQA [24 layers, 2 beams, 4096 slots, 128] fp16 with the two
+    beams swapped, and StarCoder2-7B-like GQA [32, 8 beams, 4 heads, 2048, 128] bf16
+    with every beam taking another's cache.  Moved bytes (read + write of the changed
+    rows' keys and values) per second."""
+    import torch
+    out = {}
+    for name, shape, dtype, parents in (
+            ("kv_reorder_1b_mqa", (24, 2, 4096, 128), torch.float16, [1, 0]),
+            ("kv_reorder_8b_gqa", (32, 8, 4, 2048, 128), torch.bfloat16, [1, 0, 3, 2, 5, 4, 7, 6])):
+        keys = torch.randn(shape, device=dev).to(dtype)
+        values = torch.randn(shape, device=dev).to(dtype)
+        p = torch.tensor(parents, dtype=torch.int64, device=dev)
+        length = shape[-2]
+        us = graph_time_us(lambda: sv.ops.kv_reorder(keys, values, p, length), reps=10, per_graph=4)
+        changed = sum(1 for r, q in enumerate(parents) if q != r)
+        moved = 2 * 2 * changed * keys[:, 0].numel() * keys.element_size()
+        out[name + "_us"] = us
+        out[name + "_GBps"] = moved / (us * 1e-6) / 1e9
+        del keys, values
     return out
 
 
@@ -534,24 +566,34 @@ def _graph_time_ranks(fn, dev, steps):
     return float(t[0])
 
 
+def cfg5_sample_rows(dev, cols=None):
+    """Config 5's sampling rows: 256 x V fp32 N(0,2^2) logits (columns `cols` of
+    them), uniforms, and the rows' 16384-token histories as a packed seen bitmap
+    over the whole vocabulary (the same data on every rank)."""
+    import torch
+    rows = 256
+    g = np.random.default_rng(5)
+    x = (2.0 * g.standard_normal((rows, V))).astype(np.float32)
+    ids = g.integers(0, V, (rows, 16384))
+    u = g.random(rows).astype(np.float32)
+    if cols is not None:
+        x = np.ascontiguousarray(x[:, cols])
+    seen = np.zeros((rows, V), bool)
+    seen[np.arange(rows)[:, None], ids] = True
+    packed = np.packbits(seen, axis=1, bitorder="little")  # V is a multiple of 32
+    bits = torch.from_numpy(np.ascontiguousarray(packed).view(np.int32)).to(dev)
+    return torch.from_numpy(x).to(dev), torch.from_numpy(u).to(dev), bits
+
+
 def vocab_sharded_extra(sv, dev, rank, world, steps=20):
     """Config 5's vocab-sharded sample step: 256 rows, V split across the ranks
     (slice step into the exchange block, one NCCL all-gather, merge on every rank),
     captured as one CUDA graph per rank.  Device time per step, max over ranks."""
     import torch
     import torch.distributed as dist
-    rows, cap = 256, 64
+    cap = 64
     off, w, stride = sv.sharded.slice_bounds(V, rank, world)
-    g = np.random.default_rng(5)  # the same rows on every rank
-    x = (2.0 * g.standard_normal((rows, V))).astype(np.float32)
-    ids = g.integers(0, V, (rows, 16384))
-    u = g.random(rows).astype(np.float32)
-    xd = torch.from_numpy(np.ascontiguousarray(x[:, off:off + w])).to(dev)
-    ud = torch.from_numpy(u).to(dev)
-    seen = np.zeros((rows, V), bool)
-    seen[np.arange(rows)[:, None], ids] = True
-    packed = np.packbits(seen, axis=1, bitorder="little")  # V is a multiple of 32
-    bits = torch.from_numpy(np.ascontiguousarray(packed).view(np.int32)).to(dev)
+    xd, ud, bits = cfg5_sample_rows(dev, slice(off, off + w))
     step = sv.sharded.VocabShardedSampler(xd, ud, offset=off, slice_stride=stride, seen_bits=bits,
                                           capacity=cap).capture()
     try:

@@ -444,3 +444,35 @@ def merge_beam_shards(packed, global_max, global_flags, running_scores, uniforms
         rc = L.lib().sv_merge_beam_shards(packed.data_ptr(), S, B, int(capacity), int(vocab), *tail)
         L.check(rc, "sv_merge_beam_shards")
     return o
+
+
+def kv_reorder(keys, values, parents, length, out_status=None):
+    """The beam step's KV-cache reorder in place (sv_kv_reorder,
+    runtime_shared.py:388-394): rows whose parent changed receive the parent's
+    first `length` slots.  keys / values: [layers, beams, capacity, head_dim] (MQA)
+    or [layers, beams, heads, capacity, head_dim] (GQA), the same layout each
+    (values may be None); parents: int64 [beams] on the device."""
+    _need_cuda(keys, "keys")
+    if keys.dim() == 4:
+        Lr, B, cap, D = keys.shape
+        H, sl, sb, sh, ss = 1, keys.stride(0), keys.stride(1), 0, keys.stride(2)
+    elif keys.dim() == 5:
+        Lr, B, H, cap, D = keys.shape
+        sl, sb, sh, ss = keys.stride(0), keys.stride(1), keys.stride(2), keys.stride(3)
+    else:
+        raise ValueError("keys must be [layers, beams, capacity, head_dim] or [layers, beams, heads, capacity, "
+                         "head_dim]")
+    if keys.stride(-1) != 1:
+        raise ValueError("head_dim must be contiguous")
+    if values is not None and (values.shape != keys.shape or values.stride() != keys.stride() or
+                               values.dtype != keys.dtype):
+        raise ValueError("values must have the keys' shape, strides and dtype")
+    if not 0 <= int(length) <= cap:
+        raise ValueError("length must be in [0, capacity]")
+    p = parents.reshape(-1)
+    _need_cuda(p, "parents")
+    if p.dtype != torch.int64 or not p.is_contiguous() or p.numel() != B:
+        raise ValueError("parents must be a contiguous int64 tensor [beams]")
+    rc = L.lib().sv_kv_reorder(keys.data_ptr(), _ptr(values), keys.element_size(), Lr, B, H, int(length), D, sl, sb,
+                               sh, ss, p.data_ptr(), _ptr(out_status), _stream(keys.device))
+    L.check(rc, "sv_kv_reorder")

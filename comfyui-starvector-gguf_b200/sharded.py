@@ -224,16 +224,28 @@ class VocabShardedSampler(_GraphStep):
                          slice_stride=self.stride)
 
 
+# Beam groups whose whole logits are at most this many bytes are gathered whole
+# (one all-gather, then the unsharded beam kernel on every rank) rather than
+# exchanged as slice statistics and kept lists (three collectives).
+GATHER_BEAM_BYTES = 8 << 20
+
+
 class VocabShardedBeamStep(_GraphStep):
     """The vocab-sharded beam step bound to fixed input tensors (every beam's logits
     slice, running scores, uniforms and seen bitmap, updated in place between
-    steps), with every intermediate kept, so that the whole step - the slice
-    statistics and their two all-reduces, the slice log-probs and slice step, the
-    all-gather and the merge - can be captured as one CUDA graph (capture())."""
+    steps), with every intermediate kept, so that the whole step can be captured
+    as one CUDA graph (capture()).
+
+    method "gather": one all-gather of the slices, then sv_beam_step on the whole
+    rows on every rank (for small beam groups: one collective).  method "exchange":
+    the slice statistics and their two all-reduces, the slice log-probs and slice
+    step, the all-gather of the kept lists and the merge (for rows too large to
+    gather).  "auto" gathers when the whole logits take at most GATHER_BEAM_BYTES.
+    Both give sv_beam_step's results on the whole rows."""
 
     def __init__(self, shard_logits, running_scores, uniforms, *, offset, vocab, slice_stride=None, seen_bits=None,
                  seen=None, temperature=1.5, top_p=0.9, top_k=50, keep=2, repetition_penalty=3.1, capacity=64,
-                 num_picks=None, out_capacity=0, group=None):
+                 num_picks=None, out_capacity=0, group=None, method="auto"):
         self.x, self.running, self.u = shard_logits, running_scores, uniforms
         self.device = shard_logits.device
         B, W = shard_logits.shape
@@ -245,6 +257,21 @@ class VocabShardedBeamStep(_GraphStep):
         self.num_picks, self.out_capacity = num_picks, out_capacity
         world = dist.get_world_size(group)
         dev = self.device
+        if method == "auto":
+            method = "gather" if B * world * self.stride * shard_logits.element_size() <= GATHER_BEAM_BYTES \
+                else "exchange"
+        self.method = method
+        self.out = {}
+        if method == "gather":
+            # Each rank's slice padded to the stride (-inf past the vocabulary), the
+            # gathered slices, and the whole rows they are copied back into.
+            self.send = torch.full((B, self.stride), float("-inf"), dtype=shard_logits.dtype, device=dev)
+            self.gathered = torch.empty((world, B, self.stride), dtype=shard_logits.dtype, device=dev)
+            self.whole = torch.empty((B, world * self.stride), dtype=shard_logits.dtype, device=dev)
+            self.ws = ops.beam_workspace(B, vocab, dev)
+            return
+        if method != "exchange":
+            raise ValueError("method must be 'auto', 'gather' or 'exchange'")
         self.stats = {"max": torch.empty(B, dtype=torch.float32, device=dev),
                       "flags": torch.empty(B, dtype=torch.int32, device=dev),
                       "sum": torch.empty(B, dtype=torch.int64, device=dev)}
@@ -255,9 +282,17 @@ class VocabShardedBeamStep(_GraphStep):
         self.blocks = torch.empty((world, self.block.numel()), dtype=torch.int32, device=dev)
         nbytes = ops.L.lib().sv_merge_beam_shards_workspace_bytes(B, world, capacity)
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        self.out = {}
 
     def _run(self):
+        if self.method == "gather":
+            W = self.x.shape[1]
+            self.send[:, :W].copy_(self.x)
+            dist.all_gather_into_tensor(self.gathered.view(-1), self.send.view(-1), group=self.group)
+            self.whole.view(self.beams, -1, self.stride).copy_(self.gathered.permute(1, 0, 2))
+            ops.beam_step(self.whole[:, :self.vocab], self.running, self.u, top_p=self.top_p, num_picks=self.num_picks,
+                          out_capacity=self.out_capacity, workspace=self.ws, out=self.out, **self.hist,
+                          **self.settings)
+            return
         st, g = self.stats, self.group
         ops.beam_slice_stats(self.x, out=st)
         dist.all_reduce(st["max"], op=dist.ReduceOp.MAX, group=g)

@@ -285,6 +285,29 @@ int sv_merge_beam_slices(const int32_t* blocks, int32_t shards, int32_t beams, i
                          int32_t* out_kept_count, int32_t* out_kept_idx, float* out_kept_logprob,
                          float* out_kept_prob, int32_t out_capacity, void* stream);
 
+/*
+ * Beam KV-cache reorder (replaces runtime_shared.py:388-394, CachedDecoding.reorder):
+ * every beam row r whose parent parents[r] differs from r receives its parent's
+ * keys and values over the first `length` cache slots, as the reference's
+ * keys[:, rows, ..., :length, :] = keys[:, sources, ..., :length, :] (sources read
+ * before rows are written, so swaps are safe); rows whose parent is themselves are
+ * not touched.  parents int64 [beams] in device memory (no host sync: the beam
+ * step's picks can feed it directly).  keys and values (values may be NULL) share
+ * one layout: element (layer, beam, head, slot, d) at
+ *   layer * stride_layer + beam * stride_beam + head * stride_head + slot * stride_slot + d
+ * (strides in elements; the 1B decoder's MQA cache [layers, beams, capacity, head_dim]
+ * has heads = 1, the 8B decoder's GQA cache [layers, beams, kv_heads, capacity,
+ * head_dim] heads = kv_heads).  elem_bytes 1, 2 or 4; head_dim * elem_bytes, every
+ * stride in bytes and both pointers must be multiples of 16; beams <= 8 (the
+ * node's num_beams maximum, nodes.py:128); layers * heads <= 65535;
+ * length * head_dim * elem_bytes < 2^34.  out_status (may be NULL) int32: 1 when a parent lies
+ * outside [0, beams) (its row is left as it is), else 0.  No counterpart of the
+ * kernel in the reference (it indexes with torch).
+ */
+int sv_kv_reorder(void* keys, void* values, int32_t elem_bytes, int32_t layers, int32_t beams, int32_t heads,
+                  int64_t length, int32_t head_dim, int64_t stride_layer, int64_t stride_beam, int64_t stride_head,
+                  int64_t stride_slot, const int64_t* parents, int32_t* out_status, void* stream);
+
 /* Text of a return or status code. */
 const char* sv_error_string(int32_t code);
 

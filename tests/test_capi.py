@@ -92,3 +92,26 @@ def test_loop_guard_rejects_invalid_arguments(sv):
     assert lib.sv_loop_guard(8, 2, 1, 10, 8, 64, 3, 8, None) == -2
     assert lib.sv_loop_guard(8, 4, 1, 10, 8, 2000, 3, 8, None) == -4
     assert lib.sv_loop_guard(8, 4, 0, 10, 8, 64, 3, 8, None) == -3
+
+
+def test_kv_reorder_rejects_invalid_arguments(sv):
+    """sv_kv_reorder(keys, values, elem_bytes, layers, beams, heads, length, head_dim,
+    stride_layer, stride_beam, stride_head, stride_slot, parents, out_status, stream):
+    every rejection below returns before any CUDA call."""
+    lib = sv._lib.lib()
+    base = [16, 16, 2, 24, 2, 1, 100, 128, 2 * 4096 * 128, 4096 * 128, 0, 128, 16, None, None]
+
+    def call(**kw):
+        a = list(base)
+        for k, v in kw.items():
+            a[int(k[1:])] = v
+        return lib.sv_kv_reorder(*a)
+
+    assert call(a0=None) == -1 and call(a12=None) == -1
+    assert call(a2=3) == -2
+    assert call(a4=9) == -3 and call(a4=0) == -3 and call(a3=0) == -3 and call(a6=-1) == -3
+    assert call(a3=70000) == -3                        # layers * heads > 65535
+    assert call(a6=1 << 27, a7=128) == -3               # length * head_dim * elem_bytes >= 2^34
+    assert call(a7=4) == -5                             # head_dim * elem_bytes not a multiple of 16
+    assert call(a11=12) == -5 and call(a0=24) == -5     # stride / pointer alignment
+    assert call(a6=0) == 0                              # nothing to copy: no launch

@@ -147,13 +147,17 @@ def _beam_worker(rank, world, port, q):
         out = sv.sharded.beam_step_vocab_sharded(xs, rs, us, offset=off, vocab=V, slice_stride=stride,
                                                  seen_bits=bits, capacity=CAP, out_capacity=CAP)
         res["eager"] = {k: v.cpu().numpy() for k, v in out.items()}
-        step = sv.sharded.VocabShardedBeamStep(xs, rs, us, offset=off, vocab=V, slice_stride=stride, seen_bits=bits,
-                                               capacity=CAP, out_capacity=CAP).capture()
-        for n, uu in enumerate((u, _beam_uniforms2())):
-            us.copy_(torch.from_numpy(uu))
-            out = step()
-            torch.cuda.synchronize()
-            res[f"graph{n}"] = {k: v.cpu().numpy() for k, v in out.items()}
+        for method in ("exchange", "gather"):
+            step = sv.sharded.VocabShardedBeamStep(xs, rs, us, offset=off, vocab=V, slice_stride=stride,
+                                                   seen_bits=bits, capacity=CAP, out_capacity=CAP,
+                                                   method=method).capture()
+            for n, uu in enumerate((u, _beam_uniforms2())):
+                us.copy_(torch.from_numpy(uu))
+                out = step()
+                torch.cuda.synchronize()
+                res[f"{method}{n}"] = {k: v.cpu().numpy() for k, v in out.items()}
+            step.release()
+            step = None
         q.put((rank, res))
     finally:
         if step is not None:
@@ -181,7 +185,8 @@ def _check_beam(g, ref):
 
 def test_vocab_sharded_beam_step_across_gpus():
     """The beam step with every beam's vocabulary split across the GPUs: two
-    all-reduces (the log_softmax statistics) and one all-gather."""
+    all-reduces (the log_softmax statistics) and one all-gather of the kept lists,
+    or one all-gather of the slices and the whole-row beam kernel."""
     world = min(torch.cuda.device_count(), 8)
     got = _run(_beam_worker, world)
     x, seen, running, u = _beam_data()
@@ -190,5 +195,6 @@ def test_vocab_sharded_beam_step_across_gpus():
     ref2 = O.beam(x, running, _beam_uniforms2(), **kw)
     for rank in range(world):
         _check_beam(got[rank]["eager"], ref)
-        _check_beam(got[rank]["graph0"], ref)
-        _check_beam(got[rank]["graph1"], ref2)
+        for method in ("exchange", "gather"):
+            _check_beam(got[rank][f"{method}0"], ref)
+            _check_beam(got[rank][f"{method}1"], ref2)
