@@ -435,6 +435,7 @@ def run_ours(args, rank, world, local_rank):
     extras = latency_extras(sv, dev) if rank == 0 and not args.no_extras else {}
     if rank == 0 and not args.no_extras:
         extras.update(kv_extras(sv, dev))
+        extras.update(dropin_extras(sv, dev))
     if world > 1 and not args.no_extras:
         extras.update(vocab_sharded_extra(sv, dev, rank, world))  # every rank takes part
         extras.update(vocab_sharded_beam_extra(sv, dev, rank, world))
@@ -546,6 +547,96 @@ def kv_extras(sv, dev):
         out[name + "_us"] = us
         out[name + "_GBps"] = moved / (us * 1e-6) / 1e9
         del keys, values
+    return out
+
+
+class _NoOpDecoding:
+    """A scripted decoder for timing the drop-in's loops per token: `step` replays a
+    CUDA graph that only stores the fed tokens (the decoder's own work left out) and
+    returns fixed N(0, 2^2) logits over V; the beam cache is a GPTBigCode-1B-shaped
+    MQA cache [24, beams, capacity, 128] fp16 that the loop reorders on the device
+    (sv_kv_reorder) through `reorder_device`.  The three lowest-logit ids serve as
+    eos / stop ids, so no generation ends before max_new_tokens."""
+
+    def __init__(self, rows, capacity, dev, vocab=V, seed=7):
+        import torch
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.logits = torch.randn((rows, vocab), generator=g, device=dev) * 2
+        low = torch.argsort(self.logits[0])[:3].tolist()
+        self.eos_id, self.stop_ids = low[0], low[1:]
+        self.tokens = torch.zeros(rows, dtype=torch.int64, device=dev)
+        self.fed = torch.zeros(rows, dtype=torch.int64, device=dev)
+        self.keys = torch.zeros((24, rows, capacity, 128), dtype=torch.float16, device=dev) if rows > 1 else None
+        self.values = torch.zeros_like(self.keys) if rows > 1 else None
+        self.length = 0
+        self.graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.fed.copy_(self.tokens)
+        torch.cuda.current_stream().wait_stream(s)
+        with torch.cuda.graph(self.graph):
+            self.fed.copy_(self.tokens)
+
+    def prefill(self, embeddings, rows, capacity):
+        self.length = embeddings.shape[1]
+        return self, self.logits
+
+    def step(self, tokens):
+        self.tokens.copy_(tokens)
+        self.graph.replay()
+        self.length += 1
+        return self.logits
+
+    def reorder_device(self, parents):
+        import __graft_entry__
+        __graft_entry__.load_package().kv_reorder(self.keys, self.values, parents, self.length)
+
+
+def dropin_extras(sv, dev, tokens=512, reps=3):
+    """Host-inclusive microseconds per token of the drop-in's `_sample` and
+    `_beam_sample` (2 and 8 beams) over the no-op decoder: every kernel launch,
+    ctypes call, record read and host replay of a max_new_tokens=512 generation at
+    V=49152, wall clock / tokens.  Also the same loops read back every step
+    (`_SYNC_EVERY` = 1) to show what the 16-step blocks save, and the cost of the
+    decode steps a block issues past an end (0..15, 7.5 on average: each a whole
+    loop step plus the decoder's own step)."""
+    import importlib
+    import time
+    import torch
+    rs = importlib.import_module(sv.__name__ + ".runtime_shared")
+    out = {}
+    prefix = torch.zeros((1, 300, 4), device=dev)
+    for beams in (1, 2, 8):
+        for every in (rs._SYNC_EVERY, 1):
+            saved = rs._SYNC_EVERY
+            rs._SYNC_EVERY = every
+            try:
+                times = []
+                for r in range(reps + 1):
+                    dec = _NoOpDecoding(beams, prefix.shape[1] + tokens, dev)
+                    torch.cuda.synchronize()
+                    t0 = time.perf_counter()
+                    with torch.inference_mode():
+                        if beams == 1:
+                            gen, reason = rs._sample(dec, prefix, tokens, 1.5, 0.9, dec.stop_ids, dec.eos_id, True,
+                                                     lambda step: None)
+                        else:
+                            gen, reason = rs._beam_sample(dec, prefix, tokens, 1.5, 0.9, beams, dec.stop_ids,
+                                                          dec.eos_id, True, lambda step: None)
+                    torch.cuda.synchronize()
+                    if r:  # the first run warms the caches (pinned buffers, workspaces)
+                        times.append((time.perf_counter() - t0) / tokens * 1e6)
+                    assert reason == "token_limit" and len(gen) == tokens, (reason, len(gen))
+            finally:
+                rs._SYNC_EVERY = saved
+            name = "dropin_sample" if beams == 1 else f"dropin_beam{beams}"
+            out[name + ("_us_per_token" if every > 1 else "_sync_every_step_us_per_token")] = min(times)
+    for name in ("dropin_sample", "dropin_beam2", "dropin_beam8"):
+        out[name + "_overrun_us_mean"] = 7.5 * out[name + "_us_per_token"]
+    out["dropin_config"] = (f"max_new_tokens={tokens}, V={V} fp32, loop guard on, no-op decoder step (CUDA graph), "
+                            f"1B-shaped KV cache reordered on the device for beams; wall clock incl. all host work, "
+                            f"best of {reps}")
     return out
 
 

@@ -13,8 +13,8 @@ load it by path, e.g. through __graft_entry__.load_package(), which registers it
 `starvector_b200`.
 """
 from . import _lib, sharded
-from .ops import (beam_step, beam_workspace, loop_guard, merge_beam_shards, merge_shards, penalize, sample_step,
-                  seen_bitmap, seen_reorder, seen_update)
+from .ops import (beam_advance, beam_step, beam_workspace, kv_reorder, loop_guard, merge_beam_shards, merge_shards,
+                  penalize, sample_step, seen_bitmap, seen_reorder, seen_update)
 
-__all__ = ["sample_step", "beam_step", "beam_workspace", "loop_guard", "merge_beam_shards", "merge_shards",
-           "penalize", "seen_bitmap", "seen_reorder", "seen_update", "sharded"]
+__all__ = ["sample_step", "beam_step", "beam_workspace", "beam_advance", "kv_reorder", "loop_guard",
+           "merge_beam_shards", "merge_shards", "penalize", "seen_bitmap", "seen_reorder", "seen_update", "sharded"]

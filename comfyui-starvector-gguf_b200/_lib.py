@@ -43,6 +43,8 @@ _SIGNATURES = {
     "sv_merge_beam_slices": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _D, _I32, _I32, _P, _SZ,
                                     _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P]),
     "sv_kv_reorder": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I64, _I32, _I64, _I64, _I64, _I64, _P, _P, _P]),
+    "sv_beam_advance": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _I32, _I64, _P, _P, _P, _P, _P, _P,
+                               _P, _I64, _P, _P, _I64, _P]),
     "sv_error_string": (C.c_char_p, [_I32]),
     "sv_abi_version": (_I32, []),
 }

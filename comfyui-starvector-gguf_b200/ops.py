@@ -246,6 +246,28 @@ def seen_reorder(src, dst, parents, tokens, vocab):
     L.check(rc, "sv_seen_reorder")
 
 
+def beam_advance(step_out, *, beams, vocab, step, last, stop_ids, eos_id, tails_in, tails_out, running_out,
+                 parents_out, tokens_out, seen_in=None, seen_out=None, hist_in=None, hist_out=None):
+    """The beam loop's next-step decision on the device (sv_beam_advance,
+    runtime_shared.py:237-259): from one beam_step's outputs `step_out` (picks,
+    scores, n, status) writes the next running scores, the chosen parents and
+    tokens, the rows' advanced stop-id tails and (optionally) the reordered seen
+    bitmaps and token histories.  stop_ids: int64 [S] on the device (S <= 16); tails
+    int64 [beams, S]; hist int32 [beams, capacity > step]; eos_id None never matches."""
+    picks, scores = step_out["picks"], step_out["scores"]
+    _need_cuda(picks, "picks")
+    S = stop_ids.numel() if stop_ids is not None else 0
+    words = (int(vocab) + 31) // 32
+    rc = L.lib().sv_beam_advance(
+        picks.data_ptr(), scores.data_ptr(), step_out["n"].data_ptr(), step_out["status"].data_ptr(), int(beams),
+        int(vocab), picks.numel(), int(step), int(bool(last)), _ptr(stop_ids) if S else None, S,
+        -1 if eos_id is None else int(eos_id), _ptr(tails_in) if S else None, _ptr(tails_out) if S else None,
+        running_out.data_ptr(), parents_out.data_ptr(), tokens_out.data_ptr(), _ptr(seen_in), _ptr(seen_out),
+        seen_in.stride(0) if seen_in is not None else words, _ptr(hist_in), _ptr(hist_out),
+        hist_in.stride(0) if hist_in is not None else 0, _stream(picks.device))
+    L.check(rc, "sv_beam_advance")
+
+
 def block_len(rows, capacity):
     """int32 values of one rank's slice block (the sv_merge_slices layout)."""
     return 2 * rows * capacity + 2 * rows

@@ -20,6 +20,8 @@ for the same seed.  Logits must live on a CUDA device.
 """
 from __future__ import annotations
 
+from array import array
+
 import torch
 
 from . import _lib as L
@@ -149,6 +151,91 @@ def _sample(decoder, embeddings, max_new_tokens, temperature, top_p, stop_ids, e
     return tokens, 'token_limit'
 
 
+# Stop sequences up to this many tokens are matched on the device (sv_beam_advance).
+_MAX_STOP = 16
+
+
+def _node_tokens(node, limit=None):
+    """The tokens of a candidate held as a linked node (token, parent node), oldest
+    first; only the last `limit` when given."""
+    out = []
+    while node is not None and (limit is None or len(out) < limit):
+        out.append(node[0])
+        node = node[1]
+    out.reverse()
+    return out
+
+
+def _node_ends(node, stop_ids, eos_id):
+    """_ends (runtime_shared.py:190-191) of a candidate node: its last token is
+    eos_id, or its last len(stop_ids) tokens equal stop_ids."""
+    if node[0] == eos_id:
+        return True
+    return len(stop_ids) > 0 and _node_tokens(node, len(stop_ids)) == stop_ids
+
+
+def _device_reorder(decoding, beams):
+    """A function applying device-resident parents to the decoder's cache, or None
+    when the decoder only takes host lists.  Decoders may offer
+    `reorder_device(parents)`; the reference's own CachedDecoding
+    (runtime_shared.py:388-394) is reordered by sv_kv_reorder on its keys and
+    values, which is what its `reorder` does with torch indexing."""
+    fn = getattr(decoding, "reorder_device", None)
+    if callable(fn):
+        return fn
+    keys, values, length = (getattr(decoding, name, None) for name in ("keys", "values", "length"))
+    if type(decoding).__name__ != "CachedDecoding" or not isinstance(length, int):
+        return None
+    if not (isinstance(keys, torch.Tensor) and isinstance(values, torch.Tensor) and keys.is_cuda
+            and keys.dim() in (4, 5) and keys.shape[1] == beams):
+        return None
+    try:  # identity parents: checks the cache layout, copies nothing
+        ops.kv_reorder(keys, values, torch.arange(beams, device=keys.device), length)
+    except (ValueError, RuntimeError):
+        return None
+    return lambda parents: ops.kv_reorder(decoding.keys, decoding.values, parents, decoding.length)
+
+
+class _BeamRecord:
+    """Per-step device records of a beam generation: the beam step's picks, scores,
+    pick count and status, the device's decision (running scores, parents, tokens)
+    and the loop-guard verdicts; with pinned host buffers for one block of steps."""
+
+    _PINNED = {}
+
+    def __init__(self, steps, beams, picks, block, device):
+        self.picks = torch.full((steps, picks), -1, dtype=torch.int64, device=device)
+        self.scores = torch.zeros((steps, picks), dtype=torch.float32, device=device)
+        self.n = torch.zeros(steps, dtype=torch.int32, device=device)
+        self.status = torch.zeros(steps, dtype=torch.int32, device=device)
+        self.running = torch.zeros((steps + 1, beams), dtype=torch.float32, device=device)
+        self.parents = torch.zeros((steps, beams), dtype=torch.int64, device=device)
+        self.tokens = torch.zeros((steps, beams), dtype=torch.int64, device=device)
+        self.verdict = torch.zeros(steps, dtype=torch.uint8, device=device)
+        key = (block, beams, picks)
+        if key not in self._PINNED:
+            self._PINNED[key] = {name: torch.empty((block, *t.shape[1:]), dtype=t.dtype, pin_memory=True)
+                                 for name, t in self._arrays().items()}
+        self.host = self._PINNED[key]
+
+    def _arrays(self):
+        return {"picks": self.picks, "scores": self.scores, "n": self.n, "status": self.status,
+                "running": self.running[1:], "parents": self.parents, "tokens": self.tokens,
+                "verdict": self.verdict}
+
+    def step_out(self, step):
+        return {"picks": self.picks[step], "scores": self.scores[step], "n": self.n[step:step + 1],
+                "status": self.status[step:step + 1]}
+
+    def read(self, first, last, device):
+        """Host lists of steps [first, last], after one stream synchronisation."""
+        k = last + 1 - first
+        for name, t in self._arrays().items():
+            self.host[name][:k].copy_(t[first:last + 1], non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        return {name: h[:k].tolist() for name, h in self.host.items()}
+
+
 def _beam_sample(decoder, embeddings, max_new_tokens, temperature, top_p, beams, stop_ids, eos_id, loop_guard,
                  on_step, uniforms=None):
     """Transformers' beam sampling with early_stopping=True for one prompt (runtime_shared.py:214-265).
@@ -156,65 +243,118 @@ def _beam_sample(decoder, embeddings, max_new_tokens, temperature, top_p, beams,
     Each step samples 2 * beams continuations without replacement from all beams.
     Only the first `beams` samples may finish; the best unfinished samples continue.
     Finished scores use the length penalty.
+
+    The step's decision - which candidates continue, their running scores, parents
+    and tokens, the seen bitmaps and the rows' token histories - is taken on the
+    device (sv_beam_advance), and the decoder's cache is reordered from the device
+    parents, so no step waits for the host.  The host reads the steps' records once
+    every 16 steps and replays the reference's bookkeeping over them in order (the
+    finished list with the length penalty in float64, the stop tests, the progress
+    callback, the loop guard), checking the device's decision step by step, so the
+    result, stop reason, callbacks and errors are the reference's.  Up to 15 decode
+    steps issued after an end inside a block are discarded.  A decoder whose cache
+    can only be reordered from a host list is driven one step at a time.
     """
     keep = 2 * beams
     decoding, logits = decoder.prefill(embeddings, beams, embeddings.shape[1] + max_new_tokens)
     device, vocab = logits.device, logits.shape[-1]
+    steps = max_new_tokens
     if uniforms is None:
-        uniforms = torch.rand((max_new_tokens, keep), dtype=torch.float32, device=device)
-    running = [[] for _ in range(beams)]
-    running_scores = [0.] + [-1e9] * (beams - 1)
-    seen, seen_next = ops.seen_bitmap(beams, vocab, device), ops.seen_bitmap(beams, vocab, device)
+        uniforms = torch.rand((steps, keep), dtype=torch.float32, device=device)
+    # A stop list that is not a list never equals a list slice in the reference.
+    n_stop = len(stop_ids) if isinstance(stop_ids, list) else 0
+    if n_stop > _MAX_STOP:
+        raise ValueError(f"stop sequences longer than {_MAX_STOP} tokens are not supported")
+    reorder_cache = _device_reorder(decoding, beams)
+    every = _SYNC_EVERY if reorder_cache is not None else 1
+    rec = _BeamRecord(steps, beams, keep, every, device)
+    rec.running[0, 1:] = -1e9
+    stop_dev = torch.tensor(stop_ids, dtype=torch.int64, device=device) if n_stop else None
+    tails = torch.full((2, beams, max(n_stop, 1)), -1, dtype=torch.int64, device=device)
+    seen = (ops.seen_bitmap(beams, vocab, device), ops.seen_bitmap(beams, vocab, device))
+    hist = torch.zeros((2, beams, steps), dtype=torch.int32, device=device) if loop_guard else None
+    workspace = ops.beam_workspace(beams, vocab, device)
+
+    # The reference's host state, with candidates as linked nodes (token, parent).
+    running = [None] * beams
     finished = []
     improvable = True
-    host = torch.empty(2 * keep + 2, dtype=torch.float64, pin_memory=True)
-    out = {}
-    for step in range(max_new_tokens):
-        scores_t = torch.tensor(running_scores, dtype=torch.float32, device=device)
-        out = ops.beam_step(logits.reshape(-1, vocab), scores_t, uniforms[step], seen_bits=seen,
-                            temperature=temperature, top_p=top_p, top_k=TOP_K, keep=2,
-                            repetition_penalty=REPETITION_PENALTY, num_picks=keep, out=out)
-        # One device->host transfer for picks, picked scores, count and status.
-        packed = torch.cat((out["picks"].double(), out["scores"].double(), out["n"].double(),
-                            out["status"].double()))
-        host.copy_(packed, non_blocking=True)
-        torch.cuda.current_stream(device).synchronize()
-        vals = host.tolist()
-        n, status = int(vals[2 * keep]), int(vals[2 * keep + 1])
-        if status:
-            _raise_status(status)
-        picks = [int(v) for v in vals[:n]]
-        picked = vals[keep:keep + n]  # float32 scores, exact as doubles (:236)
-        parents, tokens = zip(*(divmod(pick, vocab) for pick in picks))
-        candidates = [running[parent] + [token] for parent, token in zip(parents, tokens)]
-        last = step + 1 == max_new_tokens
-        hits = [last or _ends(candidate, stop_ids, eos_id) for candidate in candidates]
-        if improvable and len(finished) < beams:
-            finished += [(picked[j] / (step + 1) ** LENGTH_PENALTY, candidates[j])
-                         for j in range(min(beams, len(picked))) if hits[j]]
-            finished = sorted(finished, key=lambda item: item[0], reverse=True)[:beams]
-        live = [score - 1e9 * hit for score, hit in zip(picked, hits)]
-        order = sorted(range(len(picked)), key=live.__getitem__, reverse=True)[:beams]
-        running_scores = [live[j] for j in order] + [-1e9] * (beams - len(order))
-        order += [order[0]] * (beams - len(order))
-        running = [candidates[j] for j in order]
-        on_step(step + 1)
-        worst = min(score for score, _ in finished) if len(finished) == beams else -1e9
-        improvable = improvable and running_scores[0] / (step + 1) ** LENGTH_PENALTY > worst
-        if not improvable or len(finished) == beams or all(hits):
-            break
-        if loop_guard and step % 16 == 15 and _repeating(running[0], device):
-            return (finished[0][1] if finished else running[0]), 'repetition'
-        selected = torch.tensor([parents[j] for j in order], dtype=torch.int64, device=device)
-        next_tokens = torch.tensor([tokens[j] for j in order], dtype=torch.int64, device=device)
-        ops.seen_reorder(seen, seen_next, selected, next_tokens, vocab)
-        seen, seen_next = seen_next, seen
-        decoding.reorder([parents[j] for j in order])
-        logits = decoding.step(next_tokens)
-    if not finished:
-        return running[0], 'token_limit'
-    best = finished[0][1]
-    return best, ('token_limit' if len(best) == max_new_tokens and not _ends(best, stop_ids, eos_id) else 'stop')
+
+    def result(reason=None):
+        if reason == 'repetition':
+            return _node_tokens(finished[0][1] if finished else running[0]), reason
+        if not finished:
+            return _node_tokens(running[0]), 'token_limit'
+        best = _node_tokens(finished[0][1])
+        return best, ('token_limit' if len(best) == steps and not _ends(best, stop_ids, eos_id) else 'stop')
+
+    def replay(first, last_step):
+        """The reference's bookkeeping (runtime_shared.py:237-256) over steps
+        [first, last_step]; returns (result or None, the last step's parents)."""
+        nonlocal running, finished, improvable
+        h = rec.read(first, last_step, device)
+        selected = None
+        for k, step in enumerate(range(first, last_step + 1)):
+            n, status = h["n"][k], h["status"][k]
+            if status:
+                _raise_status(status)
+            picked = h["scores"][k][:n]
+            parents, tokens = zip(*(divmod(pick, vocab) for pick in h["picks"][k][:n]))
+            candidates = [(token, running[parent]) for parent, token in zip(parents, tokens)]
+            last = step + 1 == steps
+            hits = [last or _node_ends(candidate, stop_ids, eos_id) for candidate in candidates]
+            if improvable and len(finished) < beams:
+                finished += [(picked[j] / (step + 1) ** LENGTH_PENALTY, candidates[j])
+                             for j in range(min(beams, len(picked))) if hits[j]]
+                finished = sorted(finished, key=lambda item: item[0], reverse=True)[:beams]
+            live = [score - 1e9 * hit for score, hit in zip(picked, hits)]
+            order = sorted(range(len(picked)), key=live.__getitem__, reverse=True)[:beams]
+            running_scores = [live[j] for j in order] + [-1e9] * (beams - len(order))
+            order += [order[0]] * (beams - len(order))
+            running = [candidates[j] for j in order]
+            selected = [parents[j] for j in order]
+            if (selected != h["parents"][k] or [tokens[j] for j in order] != h["tokens"][k]
+                    or array('f', running_scores).tolist() != h["running"][k]):
+                raise RuntimeError(f"beam step {step}: the device's decision differs from the host replay")
+            on_step(step + 1)
+            worst = min(score for score, _ in finished) if len(finished) == beams else -1e9
+            improvable = improvable and running_scores[0] / (step + 1) ** LENGTH_PENALTY > worst
+            if not improvable or len(finished) == beams or all(hits):
+                return result(), selected
+            if loop_guard and step % 16 == 15 and h["verdict"][k]:
+                return result('repetition'), selected
+        return None, selected
+
+    synced = 0
+    for step in range(steps):
+        cur, nxt = step % 2, 1 - step % 2
+        out = rec.step_out(step)
+        ops.beam_step(logits.reshape(-1, vocab), rec.running[step], uniforms[step], seen_bits=seen[cur],
+                      temperature=temperature, top_p=top_p, top_k=TOP_K, keep=2,
+                      repetition_penalty=REPETITION_PENALTY, num_picks=keep, workspace=workspace, out=out)
+        last = step + 1 == steps
+        ops.beam_advance(out, beams=beams, vocab=vocab, step=step, last=last, stop_ids=stop_dev, eos_id=eos_id,
+                         tails_in=tails[cur], tails_out=tails[nxt], running_out=rec.running[step + 1],
+                         parents_out=rec.parents[step], tokens_out=rec.tokens[step], seen_in=seen[cur],
+                         seen_out=seen[nxt], hist_in=None if hist is None else hist[cur],
+                         hist_out=None if hist is None else hist[nxt])
+        if loop_guard and step % 16 == 15 and step + 1 >= LOOP_WINDOW * LOOP_REPEATS:
+            # running[0]'s tokens after this step (runtime_shared.py:254); shorter
+            # histories never repeat (the verdict stays 0).
+            ops.loop_guard(hist[nxt, 0:1, :step + 1], None, LOOP_WINDOW, LOOP_REPEATS,
+                           out=rec.verdict[step:step + 1])
+        if step % every == every - 1 or last:
+            done, selected = replay(synced, step)
+            if done is not None:
+                return done
+            synced = step + 1
+        if not last:
+            if reorder_cache is not None:
+                reorder_cache(rec.parents[step])
+            else:
+                decoding.reorder(selected)
+            logits = decoding.step(rec.tokens[step])
+    raise AssertionError("the last step always ends the loop")  # every candidate hits at the last step
 
 
 def install(module) -> None:

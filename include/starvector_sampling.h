@@ -308,6 +308,37 @@ int sv_kv_reorder(void* keys, void* values, int32_t elem_bytes, int32_t layers, 
                   int64_t length, int32_t head_dim, int64_t stride_layer, int64_t stride_beam, int64_t stride_head,
                   int64_t stride_slot, const int64_t* parents, int32_t* out_status, void* stream);
 
+/*
+ * The beam loop's per-step decision on the device (replaces the host bookkeeping
+ * of runtime_shared.py:237-259 that decides the next step; the finished list, stop
+ * tests and loop guard stay with the caller).  Inputs are one sv_beam_step's
+ * outputs (picks beam * vocab + token, pick_scores, n_picks, status; num_picks
+ * slots).  With hits[j] = last || token_j == eos_id || the candidate (parent row's
+ * tokens + token_j, step + 1 long) ends with stop_ids[0..n_stop), live[j] =
+ * (double)pick_scores[j] - 1e9 * hits[j] and order = the first `beams` picks by
+ * live descending (ties in pick order), padded with order[0]:
+ *   running_out[r] = (float)live[order[r]] (or -1e9 past the n picks),
+ *   parents_out[r] = parent of order[r], tokens_out[r] = token of order[r],
+ *   tails_out[r]   = tails_in[parent] shifted by one, token appended
+ *                    (tails int64 [beams, n_stop], each running row's last n_stop
+ *                    tokens, -1 before the sequence starts; unused when n_stop = 0),
+ *   seen_out[r]    = seen_in[parent] with the token's bit set (optional: both NULL
+ *                    to skip; packed bitmaps, row stride seen_stride_words),
+ *   hist_out[r]    = hist_in[parent][0, step) then the token (optional: both NULL
+ *                    to skip; int32 rows of hist_stride > step entries, the running
+ *                    rows' generated tokens, for the loop guard).
+ * A step whose status is non-zero, or without a valid pick, leaves every row its
+ * own state (parents r, tokens 0, running 0 / -1e9).  eos_id -1 never matches.
+ * beams <= num_picks <= 64, n_stop <= 16; tails_in != tails_out, hist_in != hist_out;
+ * seen_in and seen_out must not overlap.  All pointers device memory; nothing is read on the host.
+ */
+int sv_beam_advance(const int64_t* picks, const float* pick_scores, const int32_t* n_picks, const int32_t* status,
+                    int32_t beams, int32_t vocab, int32_t num_picks, int32_t step, int32_t last,
+                    const int64_t* stop_ids, int32_t n_stop, int64_t eos_id, const int64_t* tails_in,
+                    int64_t* tails_out, float* running_out, int64_t* parents_out, int64_t* tokens_out,
+                    const uint32_t* seen_in, uint32_t* seen_out, int64_t seen_stride_words, const int32_t* hist_in,
+                    int32_t* hist_out, int64_t hist_stride, void* stream);
+
 /* Text of a return or status code. */
 const char* sv_error_string(int32_t code);
 

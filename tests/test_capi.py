@@ -115,3 +115,27 @@ def test_kv_reorder_rejects_invalid_arguments(sv):
     assert call(a7=4) == -5                             # head_dim * elem_bytes not a multiple of 16
     assert call(a11=12) == -5 and call(a0=24) == -5     # stride / pointer alignment
     assert call(a6=0) == 0                              # nothing to copy: no launch
+
+
+def test_beam_advance_rejects_invalid_arguments(sv):
+    """sv_beam_advance(picks, pick_scores, n_picks, status, beams, vocab, num_picks,
+    step, last, stop_ids, n_stop, eos_id, tails_in, tails_out, running_out,
+    parents_out, tokens_out, seen_in, seen_out, seen_stride_words, hist_in, hist_out,
+    hist_stride, stream): rejections return before any CUDA call."""
+    lib = sv._lib.lib()
+    base = [16, 16, 16, 16, 2, 100, 4, 3, 0, 16, 2, -1, 16, 32, 16, 16, 16, 64, 128, 4, 256, 512, 8, None]
+
+    def call(**kw):
+        a = list(base)
+        for k, v in kw.items():
+            a[int(k[1:])] = v
+        return lib.sv_beam_advance(*a)
+
+    assert call(a0=None) == -1 and call(a14=None) == -1 and call(a16=None) == -1
+    assert call(a9=None) == -1 and call(a12=None) == -1            # stop ids without their tails
+    assert call(a18=None) == -1 and call(a21=None) == -1           # one of a pair
+    assert call(a6=65) == -3 and call(a4=5) == -3 and call(a10=17) == -3 and call(a7=-1) == -3
+    assert call(a19=3) == -3                                       # seen stride < ceil(vocab / 32)
+    assert call(a13=16) == -1 and call(a21=256) == -1              # in place
+    assert call(a22=3) == -1                                       # history row shorter than step + 1
+    assert call(a18=70) == -1                                      # seen_out overlaps seen_in

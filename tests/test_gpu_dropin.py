@@ -179,3 +179,107 @@ def test_error_status_inside_a_read_block(rs):
     assert events == list(range(1, 10))
     fed = [c[1][0] for c in decoder.calls if c[0] == "step"]
     assert fed == [7] * 9 + [0] + [7] * 5  # the failed step 9 is fed as token 0
+
+
+class CachedDecoding:
+    """A scripted decoder with the reference's CachedDecoding cache protocol
+    (runtime_shared.py:345-394): keys / values [layers, rows, capacity, head_dim],
+    `length`, `reorder(parents)` by torch indexing.  The drop-in recognises the
+    class and reorders the cache on the device from device parents.  Each step
+    writes the fed token into its cache slot, so the final cache records every
+    row's ancestry; logits are seeded per step (random, so beams branch); fed ids
+    are checked on the device (no host sync)."""
+
+    def __init__(self, vocab=64, context=200, rows=2, seed=0, never=()):
+        self.vocab, self.context, self.seed = vocab, context, seed
+        self.never = torch.tensor(list(never), dtype=torch.int64, device=DEV)
+        self.bad = torch.zeros((), dtype=torch.bool, device=DEV)
+
+    def embed(self, ids):
+        return torch.zeros((*ids.shape, 4), device=DEV)
+
+    def prefill(self, embeddings, rows, capacity):
+        self.rows, self.length, self.index = rows, embeddings.shape[1], 0
+        self.keys = torch.zeros((2, rows, capacity, 8), device=DEV)
+        self.values = torch.zeros_like(self.keys)
+        # Every step's logits made up front, so a step launches no random kernels.
+        g = torch.Generator(device=DEV).manual_seed(self.seed)
+        self.table = torch.randn((capacity - self.length + 1, rows, self.vocab), generator=g, device=DEV) * 3
+        self.table[:, :, self.never] = -60.  # ids that are never drawn
+        return self, self._logits()
+
+    def _logits(self):
+        return self.table[self.index]
+
+    def step(self, tokens):
+        self.bad |= ((tokens < 0) | (tokens >= self.vocab)).any()
+        self.keys[:, :, self.length, 0] = tokens.float()
+        self.values[:, :, self.length, 1] = tokens.float() + 0.5
+        self.length += 1
+        self.index += 1
+        return self._logits()
+
+    def reorder(self, parents):
+        rows = [row for row, parent in enumerate(parents) if parent != row]
+        if rows:
+            sources = [parents[row] for row in rows]
+            self.keys[:, rows, ..., :self.length, :] = self.keys[:, sources, ..., :self.length, :]
+            self.values[:, rows, ..., :self.length, :] = self.values[:, sources, ..., :self.length, :]
+
+
+class HostDecoding(CachedDecoding):
+    """The same decoder under another name: the drop-in reorders it from host lists,
+    one step at a time."""
+
+
+@pytest.mark.parametrize("beams", [2, 3, 8])
+@pytest.mark.parametrize("loop_guard", [True, False])
+def test_device_decision_equals_host_path(rs, beams, loop_guard):
+    """The 16-step device-driven loop and the per-step host-driven loop give the same
+    tokens, reason, callbacks and final cache (stop ids and eos drawn by chance from
+    64 tokens, so generations end at varied steps)."""
+    for seed in range(6):
+        runs = []
+        for cls in (CachedDecoding, HostDecoding):
+            decoder, events = cls(seed=seed), []
+            svg, reason = generate(rs, decoder, torch.zeros(1, 8, 4, device=DEV), max_new_tokens=150,
+                                   num_beams=beams, loop_guard=loop_guard, progress_callback=events.append, seed=seed)
+            assert not bool(decoder.bad)
+            runs.append((svg, reason, events, decoder.keys[:, :, :decoder.length].clone(),
+                         decoder.values[:, :, :decoder.length].clone()))
+        (s1, r1, e1, k1, v1), (s2, r2, e2, k2, v2) = runs
+        assert (s1, r1, e1) == (s2, r2, e2)
+        # The device loop may run up to 15 steps past the end: compare the slots
+        # both wrote.
+        n = min(k1.shape[2], k2.shape[2])
+        assert torch.equal(k1[:, :, :n], k2[:, :, :n]) and torch.equal(v1[:, :, :n], v2[:, :, :n])
+
+
+def test_beam_loop_syncs_once_per_block(rs):
+    """With a decoder reordered on the device, the beam loop's host synchronisations
+    are one per 16 steps (plus setup), not one per token."""
+    import traceback
+    import warnings
+    decoder = CachedDecoding(vocab=4096, context=200, seed=3, never=[4000, 4001, 4002])
+    steps = 96
+    sites = []
+
+    def record(message, category, filename, lineno, file=None, line=None):
+        if "called a synchronizing" in str(message):
+            frames = [f for f in traceback.extract_stack()[:-1] if not f.filename.endswith("warnings.py")]
+            sites.append(" < ".join(f"{f.filename.rsplit('/', 1)[-1]}:{f.lineno}" for f in frames[-3:][::-1]))
+
+    torch.cuda.synchronize()
+    with warnings.catch_warnings():
+        warnings.simplefilter("always")
+        warnings.showwarning = record
+        torch.cuda.set_sync_debug_mode("warn")
+        try:
+            embeddings = torch.zeros(1, 10, 4, device=DEV)
+            with torch.inference_mode():
+                generated, reason = rs._beam_sample(decoder, embeddings, steps, 1.5, 0.9, 2, [4000, 4001], 4002,
+                                                    False, lambda step: None)
+        finally:
+            torch.cuda.set_sync_debug_mode("default")
+    assert reason == "token_limit" and len(generated) == steps
+    assert steps // 16 <= len(sites) <= steps // 16 + 3, sorted(set(sites))
