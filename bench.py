@@ -435,6 +435,7 @@ def run_ours(args, rank, world, local_rank):
     extras = latency_extras(sv, dev) if rank == 0 and not args.no_extras else {}
     if rank == 0 and not args.no_extras:
         extras.update(kv_extras(sv, dev))
+        extras.update(guard_extras(sv, dev))
         extras.update(dropin_extras(sv, dev))
     if world > 1 and not args.no_extras:
         extras.update(vocab_sharded_extra(sv, dev, rank, world))  # every rank takes part
@@ -547,6 +548,36 @@ def kv_extras(sv, dev):
         out[name + "_us"] = us
         out[name + "_GBps"] = moved / (us * 1e-6) / 1e9
         del keys, values
+    return out
+
+
+def guard_extras(sv, dev):
+    """One loop-guard check of a single growing sequence at 4096 and 16384 tokens
+    (runtime_shared.py:207, every 16 steps): the incremental guard (enter 16 new
+    windows, probe the occurrence table) against a full rescan of the row by the
+    batched kernel.  Random tokens (no repeat: the probe ends at the first empty
+    slot) and a row ending in a loop (the probe verifies three matches)."""
+    import torch
+    out = {}
+    g = np.random.default_rng(11)
+    for n in (4096, 16384):
+        for kind in ("random", "looping"):
+            row = g.integers(0, V, n)
+            if kind == "looping":
+                row[n - 64 * 3:] = np.tile(row[n - 64:], 3)
+            t = torch.from_numpy(row).to(dev)
+            table = sv.ops.guard_table(n, dev)
+            verdict = torch.zeros(1, dtype=torch.uint8, device=dev)
+            sv.ops.loop_guard_incremental(table, t, 0, n - 16, out=verdict)  # the windows already entered
+            us = graph_time_us(lambda: sv.ops.loop_guard_incremental(table, t, n - 16, n, out=verdict), reps=20,
+                               per_graph=10)
+            torch.cuda.synchronize()
+            assert bool(verdict.item()) == (kind == "looping")
+            out[f"loop_guard_incremental_{n}_{kind}_us"] = us
+        lens = torch.full((1,), n, dtype=torch.int32, device=dev)
+        v = torch.zeros(1, dtype=torch.uint8, device=dev)
+        out[f"loop_guard_rescan_{n}_us"] = graph_time_us(lambda: sv.loop_guard(t[None], lens, out=v), reps=20,
+                                                         per_graph=10)
     return out
 
 

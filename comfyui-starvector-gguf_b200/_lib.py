@@ -12,7 +12,7 @@ LIB_PATH = os.path.join(HERE, "libstarvector_sampling.so")
 
 SV_OK = 0
 SV_E_ARG, SV_E_DTYPE, SV_E_SHAPE, SV_E_RANGE, SV_E_ALIGN, SV_E_WORKSPACE, SV_E_CUDA = range(-1, -8, -1)
-ST_OK, ST_NAN, ST_POSINF, ST_ALLNEGINF, ST_HISTORY, ST_TIMEOUT, ST_SHARD_OVERFLOW = range(7)
+ST_OK, ST_NAN, ST_POSINF, ST_ALLNEGINF, ST_HISTORY, ST_TIMEOUT, ST_SHARD_OVERFLOW, ST_GUARD_FULL = range(8)
 F32, F16, BF16 = 0, 1, 2
 HIST_NONE, HIST_IDS32, HIST_IDS64, HIST_MASK8, HIST_BITS32 = range(5)
 DENSE_NONE, DENSE_SCORES, DENSE_PROBS = range(3)
@@ -44,7 +44,8 @@ _SIGNATURES = {
                                     _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P]),
     "sv_kv_reorder": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I64, _I32, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "sv_beam_advance": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _I32, _I64, _P, _P, _P, _P, _P, _P,
-                               _P, _I64, _P, _P, _I64, _P]),
+                               _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I32, _P]),
+    "sv_loop_guard_incremental": (_I32, [_P, _I64, _P, _I32, _I64, _I64, _I32, _I32, _P, _P, _P]),
     "sv_error_string": (C.c_char_p, [_I32]),
     "sv_abi_version": (_I32, []),
 }

@@ -15,7 +15,8 @@
 // writes the decision.  _ends needs only each running row's last len(stop_ids)
 // tokens, kept on the device as a tail per row and advanced here; the rows' whole
 // token histories (for the loop guard on running[0], :254) are optionally carried
-// along the same way.  The finished
+// along the same way, and so is each row's rolling window hash, whose window
+// ending at this step goes into the incremental loop guard's occurrence table.  The finished
 // list, the stop tests and the loop guard stay on the host, which replays the
 // reference's bookkeeping from the steps' records once per block of steps and
 // checks the device's parents and tokens against its own.
@@ -24,6 +25,7 @@
 #include <cstdint>
 
 #include "../../include/starvector_sampling.h"
+#include "sv_guard.cuh"
 
 namespace {
 
@@ -52,6 +54,11 @@ struct AdvanceArgs {
   const int32_t* hist_in;
   int32_t* hist_out;
   int64_t hist_stride;
+  const uint32_t* whash_in;
+  uint32_t* whash_out;
+  unsigned long long* guard_table;
+  int64_t guard_mask;
+  int window;
 };
 
 __global__ void __launch_bounds__(ANT) beam_advance_kernel(const AdvanceArgs a) {
@@ -112,6 +119,15 @@ __global__ void __launch_bounds__(ANT) beam_advance_kernel(const AdvanceArgs a) 
       a.tokens_out[r] = t;
       for (int k = 0; k < a.n_stop; ++k)
         a.tails_out[r * a.n_stop + k] = k + 1 < a.n_stop ? a.tails_in[p * a.n_stop + k + 1] : t;
+      if (a.guard_table) {
+        // The row's window ending at this step, rolled from its parent's, and its
+        // entry in the loop guard's occurrence table (sv_guard.cuh).
+        uint32_t h = a.whash_in[p] * sv::kGuardBase + sv::guard_tok((int32_t)t);
+        if (a.step >= a.window)
+          h -= sv::guard_tok(a.hist_in[p * a.hist_stride + a.step - a.window]) * sv::guard_pow(sv::kGuardBase, a.window);
+        a.whash_out[r] = h;
+        if (a.step >= a.window - 1) sv::guard_insert(a.guard_table, a.guard_mask, h, (uint32_t)(a.step - a.window + 1));
+      }
     } else {
       // A failed step (the host raises when it reads the record): every row keeps
       // its own state, the running scores restart as at the first step and the
@@ -120,6 +136,7 @@ __global__ void __launch_bounds__(ANT) beam_advance_kernel(const AdvanceArgs a) 
       a.parents_out[r] = r;
       a.tokens_out[r] = 0;
       for (int k = 0; k < a.n_stop; ++k) a.tails_out[r * a.n_stop + k] = a.tails_in[r * a.n_stop + k];
+      if (a.guard_table) a.whash_out[r] = a.whash_in[r];
     }
   }
   // The rows' state, out of place: seen_out[b] = seen_in[parent_b] with the bit of
@@ -158,7 +175,8 @@ extern "C" int sv_beam_advance(const int64_t* picks, const float* pick_scores, c
                                const int64_t* tails_in, int64_t* tails_out, float* running_out,
                                int64_t* parents_out, int64_t* tokens_out, const uint32_t* seen_in, uint32_t* seen_out,
                                int64_t seen_stride_words, const int32_t* hist_in, int32_t* hist_out,
-                               int64_t hist_stride, void* stream) {
+                               int64_t hist_stride, const uint32_t* whash_in, uint32_t* whash_out,
+                               unsigned long long* guard_table, int64_t guard_entries, int32_t window, void* stream) {
   if (!picks || !pick_scores || !n_picks || !status || !running_out || !parents_out || !tokens_out) return SV_E_ARG;
   if (n_stop > 0 && (!stop_ids || !tails_in || !tails_out)) return SV_E_ARG;
   if ((seen_in == nullptr) != (seen_out == nullptr) || (hist_in == nullptr) != (hist_out == nullptr)) return SV_E_ARG;
@@ -169,6 +187,11 @@ extern "C" int sv_beam_advance(const int64_t* picks, const float* pick_scores, c
   if (seen_in && seen_stride_words < words) return SV_E_SHAPE;
   if (tails_in && tails_in == tails_out) return SV_E_ARG;
   if (hist_in && (hist_stride <= step || hist_in == hist_out)) return SV_E_ARG;
+  if (guard_table) {
+    if (!hist_in || !whash_in || !whash_out || whash_in == whash_out) return SV_E_ARG;
+    if (guard_entries < 2 || (guard_entries & (guard_entries - 1)) || window < 1 || window > 1024) return SV_E_SHAPE;
+    if (reinterpret_cast<uintptr_t>(guard_table) % 8) return SV_E_ALIGN;
+  }
   if (seen_in) {
     const uintptr_t s0 = reinterpret_cast<uintptr_t>(seen_in), d0 = reinterpret_cast<uintptr_t>(seen_out);
     const uintptr_t span = (uintptr_t)beams * seen_stride_words * 4;
@@ -199,6 +222,11 @@ extern "C" int sv_beam_advance(const int64_t* picks, const float* pick_scores, c
   a.hist_in = hist_in;
   a.hist_out = hist_out;
   a.hist_stride = hist_stride;
+  a.whash_in = whash_in;
+  a.whash_out = whash_out;
+  a.guard_table = guard_table;
+  a.guard_mask = guard_entries - 1;
+  a.window = window;
   // One block per 4096 copied words (every block repeats the small decision).
   const int64_t items = (seen_in ? (int64_t)beams * words : 0) + (hist_in ? (int64_t)beams * (step + 1) : 0);
   int64_t blocks = (items + 4095) / 4096;

@@ -312,6 +312,7 @@ const char* sv_error_string(int32_t code) {
     case SV_ST_HISTORY: return "history id outside [0, vocab)";
     case SV_ST_TIMEOUT: return "asynchronous copy wait timed out";
     case SV_ST_SHARD_OVERFLOW: return "a vocabulary slice kept more tokens than its list holds (sample unsharded)";
+    case SV_ST_GUARD_FULL: return "the loop guard's window table is full";
     default: return "unknown code";
   }
 }

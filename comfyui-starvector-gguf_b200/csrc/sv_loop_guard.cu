@@ -14,6 +14,8 @@
 
 #include <cstdint>
 
+#include "../../include/starvector_sampling.h"
+#include "sv_guard.cuh"
 #include "sv_internal.h"
 
 namespace sv {
@@ -137,4 +139,87 @@ cudaError_t launch_loop_guard(const void* tokens, int token_bytes, int rows, int
 
 int loop_guard_max_window() { return LG_MAXW; }
 
+// ---------------------------------------------------------------------------
+// Incremental loop guard: one sequence's verdict from its window-occurrence table
+// (sv_guard.cuh) in time independent of the sequence's length.  The CTA first
+// inserts the windows ending at positions [from, L) - each thread a contiguous run,
+// the first window hashed directly, the rest rolled - then warp 0 walks the tail
+// hash's probe chain, verifying each candidate start against the tail token by
+// token, until `repeats` distinct starts match (the tail itself among them, as
+// the reference counts it) or an empty slot ends the chain.
+
+constexpr int GI_NT = 128;
+
+template <typename Tok>
+__global__ void __launch_bounds__(GI_NT) guard_incremental_kernel(unsigned long long* table, int64_t mask,
+                                                                  const Tok* __restrict__ tokens, int64_t from,
+                                                                  int64_t L, int w, int repeats, uint8_t* verdict,
+                                                                  int32_t* status) {
+  __shared__ Tok tail[LG_MAXW];
+  __shared__ int full;
+  const int tid = threadIdx.x;
+  if (tid == 0) full = 0;
+  __syncthreads();
+  const uint32_t bw = guard_pow(kGuardBase, w);
+  const int64_t e0 = from > (int64_t)w - 1 ? from : (int64_t)w - 1;
+  if (e0 < L) {
+    const int64_t n = L - e0, per = (n + GI_NT - 1) / GI_NT;
+    const int64_t a = e0 + tid * per, b = a + per < L ? a + per : L;
+    if (a < b) {
+      uint32_t h = 0;
+      for (int k = 0; k < w; ++k) h = h * kGuardBase + guard_tok(tokens[a - w + 1 + k]);
+      for (int64_t e = a; e < b; ++e) {
+        if (!guard_insert(table, mask, h, (uint32_t)(e - w + 1))) full = 1;
+        if (e + 1 < b) h = h * kGuardBase + guard_tok(tokens[e + 1]) - guard_tok(tokens[e + 1 - w]) * bw;
+      }
+    }
+  }
+  for (int k = tid; k < w && L >= w; k += GI_NT) tail[k] = tokens[L - w + k];
+  __syncthreads();
+  if (tid >= 32) return;
+  const int lane = tid;
+  int count = 0;
+  if (L >= (int64_t)w * repeats) {
+    uint32_t ht = 0;
+    for (int k = 0; k < w; ++k) ht = ht * kGuardBase + guard_tok(tail[k]);
+    int64_t slot = guard_mix(ht) & mask;
+    for (int64_t i = 0; i <= mask && count < repeats; ++i, slot = (slot + 1) & mask) {
+      const unsigned long long e = table[slot];
+      if (e == kGuardEmpty) break;
+      if ((uint32_t)(e >> 32) != ht) continue;
+      const int64_t s = (uint32_t)e;
+      bool eq = s + w <= L;
+      for (int k = lane; k < w && eq; k += 32) eq = tokens[s + k] == tail[k];
+      if (__all_sync(0xffffffffu, eq)) ++count;
+    }
+  }
+  if (lane == 0) {
+    *verdict = count >= repeats;
+    if (status) *status = full ? SV_ST_GUARD_FULL : SV_ST_OK;
+  }
+}
+
 }  // namespace sv
+
+// See include/starvector_sampling.h.
+extern "C" int sv_loop_guard_incremental(unsigned long long* table, int64_t table_entries, const void* tokens,
+                                         int32_t token_bytes, int64_t insert_from, int64_t length, int32_t window,
+                                         int32_t repeats, uint8_t* out_verdict, int32_t* out_status, void* stream) {
+  using namespace sv;
+  if (!table || !tokens || !out_verdict) return SV_E_ARG;
+  if (token_bytes != 4 && token_bytes != 8) return SV_E_DTYPE;
+  if (table_entries < 2 || (table_entries & (table_entries - 1))) return SV_E_SHAPE;
+  if (length < 0 || insert_from < 0 || insert_from > length || length > 0x7fffffffLL) return SV_E_SHAPE;
+  if (window < 1 || window > LG_MAXW || repeats < 1) return SV_E_RANGE;
+  if (reinterpret_cast<uintptr_t>(tokens) % token_bytes || reinterpret_cast<uintptr_t>(table) % 8) return SV_E_ALIGN;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (token_bytes == 4)
+    guard_incremental_kernel<int32_t><<<1, GI_NT, 0, st>>>(table, table_entries - 1,
+                                                           static_cast<const int32_t*>(tokens), insert_from, length,
+                                                           window, repeats, out_verdict, out_status);
+  else
+    guard_incremental_kernel<int64_t><<<1, GI_NT, 0, st>>>(table, table_entries - 1,
+                                                           static_cast<const int64_t*>(tokens), insert_from, length,
+                                                           window, repeats, out_verdict, out_status);
+  return cudaGetLastError() == cudaSuccess ? SV_OK : SV_E_CUDA;
+}

@@ -247,13 +247,16 @@ def seen_reorder(src, dst, parents, tokens, vocab):
 
 
 def beam_advance(step_out, *, beams, vocab, step, last, stop_ids, eos_id, tails_in, tails_out, running_out,
-                 parents_out, tokens_out, seen_in=None, seen_out=None, hist_in=None, hist_out=None):
+                 parents_out, tokens_out, seen_in=None, seen_out=None, hist_in=None, hist_out=None,
+                 whash_in=None, whash_out=None, guard_table=None, window=64):
     """The beam loop's next-step decision on the device (sv_beam_advance,
     runtime_shared.py:237-259): from one beam_step's outputs `step_out` (picks,
     scores, n, status) writes the next running scores, the chosen parents and
     tokens, the rows' advanced stop-id tails and (optionally) the reordered seen
-    bitmaps and token histories.  stop_ids: int64 [S] on the device (S <= 16); tails
-    int64 [beams, S]; hist int32 [beams, capacity > step]; eos_id None never matches."""
+    bitmaps, token histories and rolling window hashes (entering each row's window
+    in the incremental loop guard's `guard_table`).  stop_ids: int64 [S] on the
+    device (S <= 16); tails int64 [beams, S]; hist int32 [beams, capacity > step];
+    whash int32 [beams]; eos_id None never matches."""
     picks, scores = step_out["picks"], step_out["scores"]
     _need_cuda(picks, "picks")
     S = stop_ids.numel() if stop_ids is not None else 0
@@ -264,8 +267,39 @@ def beam_advance(step_out, *, beams, vocab, step, last, stop_ids, eos_id, tails_
         -1 if eos_id is None else int(eos_id), _ptr(tails_in) if S else None, _ptr(tails_out) if S else None,
         running_out.data_ptr(), parents_out.data_ptr(), tokens_out.data_ptr(), _ptr(seen_in), _ptr(seen_out),
         seen_in.stride(0) if seen_in is not None else words, _ptr(hist_in), _ptr(hist_out),
-        hist_in.stride(0) if hist_in is not None else 0, _stream(picks.device))
+        hist_in.stride(0) if hist_in is not None else 0, _ptr(whash_in), _ptr(whash_out), _ptr(guard_table),
+        0 if guard_table is None else guard_table.numel(), int(window), _stream(picks.device))
     L.check(rc, "sv_beam_advance")
+
+
+def guard_table(windows, device):
+    """An empty occurrence table for the incremental loop guard with room for
+    `windows` window entries (a power of two >= 2 x windows, all bits set)."""
+    n = 64
+    while n < 2 * windows:
+        n *= 2
+    return torch.full((n,), -1, dtype=torch.int64, device=device)
+
+
+def loop_guard_incremental(table, tokens, insert_from, length, window=64, repeats=3, out=None, status=None):
+    """Incremental loop guard (sv_loop_guard_incremental, runtime_shared.py:156-167):
+    enters the windows of `tokens` (a CUDA int32/int64 row) ending at positions
+    [insert_from, length) into `table`, then writes the verdict for the first
+    `length` tokens to `out` (uint8 [1]); returns `out`."""
+    _need_cuda(tokens, "tokens")
+    t = tokens.reshape(-1)
+    if t.dtype not in (torch.int32, torch.int64) or t.stride(0) != 1:
+        raise ValueError("tokens must be a contiguous int32 or int64 row")
+    if not 0 <= int(insert_from) <= int(length) <= t.numel():
+        raise ValueError("need 0 <= insert_from <= length <= len(tokens)")
+    if table.dtype != torch.int64 or not table.is_contiguous():
+        raise ValueError("table must be a contiguous int64 tensor (guard_table)")
+    v = out if out is not None else torch.empty(1, dtype=torch.uint8, device=t.device)
+    rc = L.lib().sv_loop_guard_incremental(table.data_ptr(), table.numel(), t.data_ptr(), t.element_size(),
+                                           int(insert_from), int(length), int(window), int(repeats), v.data_ptr(),
+                                           _ptr(status), _stream(t.device))
+    L.check(rc, "sv_loop_guard_incremental")
+    return v
 
 
 def block_len(rows, capacity):

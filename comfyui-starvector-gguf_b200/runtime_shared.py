@@ -83,35 +83,48 @@ class _TokenHistory:
 
     def __init__(self, rows, capacity, device):
         self.ids = torch.zeros((rows, max(capacity, 1)), dtype=torch.int64, device=device)
-        self.length = 0
 
     def slot(self, step):
         """Row 0's slot of a step, as the kernel's token output."""
         return self.ids[0, step:step + 1]
-
-    def repeating(self, row=0, length=None):
-        length = self.length if length is None else length
-        if length < LOOP_WINDOW * LOOP_REPEATS:
-            return False
-        lengths = torch.full((1,), length, dtype=torch.int32, device=self.ids.device)
-        return bool(ops.loop_guard(self.ids[row:row + 1], lengths, LOOP_WINDOW, LOOP_REPEATS)[0])
 
 
 # The host reads the sampled tokens once per loop-guard period (runtime_shared.py:207)
 # instead of once per token.
 _SYNC_EVERY = 16
 
+_PINNED = {}
+
+
+def _read_block(arrays, first, last, device):
+    """Host lists of rows [first, last] of device arrays (a dict), through pinned
+    buffers cached per shape and one stream synchronisation."""
+    k = last + 1 - first
+    host = {}
+    for name, t in arrays.items():
+        key = (name, t.dtype, tuple(t.shape[1:]))
+        buf = _PINNED.get(key)
+        if buf is None or buf.shape[0] < k:
+            buf = _PINNED[key] = torch.empty((max(k, _SYNC_EVERY), *t.shape[1:]), dtype=t.dtype, pin_memory=True)
+        buf[:k].copy_(t[first:last + 1], non_blocking=True)
+        host[name] = buf
+    torch.cuda.current_stream(device).synchronize()
+    return {name: buf[:k].tolist() for name, buf in host.items()}
+
 
 def _sample(decoder, embeddings, max_new_tokens, temperature, top_p, stop_ids, eos_id, loop_guard, on_step,
             uniforms=None):
     """Transformers' multinomial sampling of one sequence (runtime_shared.py:194-211).
 
-    The tokens stay on the device: the host reads them (and the steps' statuses) once
-    every 16 steps and at the last step, then goes through that block's steps in
-    order - the status check, the progress callback, the end check and, every 16th
-    step, the loop guard - exactly as the reference does per token, so the tokens,
-    the stop reason, the callbacks and the errors are the reference's.  Up to 15
-    decode steps issued after an end inside a block are discarded.
+    The tokens stay on the device: the host reads them (and the steps' statuses and
+    loop-guard verdicts) once every 16 steps and at the last step, then goes through
+    that block's steps in order - the status check, the progress callback, the end
+    check and, every 16th step, the loop guard - exactly as the reference does per
+    token, so the tokens, the stop reason, the callbacks and the errors are the
+    reference's.  The loop guard is incremental (sv_loop_guard_incremental): each
+    check enters the 16 new windows in an occurrence table and probes it for the
+    tail, in time independent of the sequence's length.  Up to 15 decode steps
+    issued after an end inside a block are discarded.
     """
     decoding, logits = decoder.prefill(embeddings, 1, embeddings.shape[1] + max_new_tokens)
     device, vocab = logits.device, logits.shape[-1]
@@ -120,6 +133,9 @@ def _sample(decoder, embeddings, max_new_tokens, temperature, top_p, stop_ids, e
     seen = ops.seen_bitmap(1, vocab, device)
     history = _TokenHistory(1, max_new_tokens, device)
     statuses = torch.zeros(max_new_tokens, dtype=torch.int32, device=device)
+    verdicts = torch.zeros(max_new_tokens, dtype=torch.uint8, device=device)
+    table = ops.guard_table(max_new_tokens, device) if loop_guard else None
+    guarded = 0  # tokens whose windows are in the table
     out = {}
     tokens = []
     synced = 0
@@ -130,18 +146,22 @@ def _sample(decoder, embeddings, max_new_tokens, temperature, top_p, stop_ids, e
         out = ops.sample_step(logits.reshape(1, vocab), uniforms[step], seen_bits=seen, temperature=temperature,
                               top_p=top_p, top_k=TOP_K, keep=1, repetition_penalty=REPETITION_PENALTY,
                               update_seen_bits=seen, out=out)
-        history.length = step + 1
+        if loop_guard and step % 16 == 15:
+            ops.loop_guard_incremental(table, history.ids[0], guarded, step + 1, LOOP_WINDOW, LOOP_REPEATS,
+                                       out=verdicts[step:step + 1])
+            guarded = step + 1
         if step % _SYNC_EVERY == _SYNC_EVERY - 1 or step + 1 == max_new_tokens:
-            block = history.ids[0, synced:step + 1].tolist()
-            block_status = statuses[synced:step + 1].tolist()
-            for j, (value, status) in enumerate(zip(block, block_status), start=synced):
+            block = _read_block({"token": history.ids[0], "status": statuses, "verdict": verdicts}, synced, step,
+                                device)
+            for j, (value, status, verdict) in enumerate(zip(block["token"], block["status"], block["verdict"]),
+                                                         start=synced):
                 if value < 0:
                     _raise_status(int(status))
                 tokens.append(value)
                 on_step(j + 1)
                 if _ends(tokens, stop_ids, eos_id):
                     return tokens, 'stop'
-                if loop_guard and j % 16 == 15 and history.repeating(length=j + 1):
+                if loop_guard and j % 16 == 15 and verdict:
                     return tokens, 'repetition'
             synced = step + 1
         if step + 1 < max_new_tokens:
@@ -199,11 +219,9 @@ def _device_reorder(decoding, beams):
 class _BeamRecord:
     """Per-step device records of a beam generation: the beam step's picks, scores,
     pick count and status, the device's decision (running scores, parents, tokens)
-    and the loop-guard verdicts; with pinned host buffers for one block of steps."""
+    and the loop-guard verdicts."""
 
-    _PINNED = {}
-
-    def __init__(self, steps, beams, picks, block, device):
+    def __init__(self, steps, beams, picks, device):
         self.picks = torch.full((steps, picks), -1, dtype=torch.int64, device=device)
         self.scores = torch.zeros((steps, picks), dtype=torch.float32, device=device)
         self.n = torch.zeros(steps, dtype=torch.int32, device=device)
@@ -212,28 +230,16 @@ class _BeamRecord:
         self.parents = torch.zeros((steps, beams), dtype=torch.int64, device=device)
         self.tokens = torch.zeros((steps, beams), dtype=torch.int64, device=device)
         self.verdict = torch.zeros(steps, dtype=torch.uint8, device=device)
-        key = (block, beams, picks)
-        if key not in self._PINNED:
-            self._PINNED[key] = {name: torch.empty((block, *t.shape[1:]), dtype=t.dtype, pin_memory=True)
-                                 for name, t in self._arrays().items()}
-        self.host = self._PINNED[key]
-
-    def _arrays(self):
-        return {"picks": self.picks, "scores": self.scores, "n": self.n, "status": self.status,
-                "running": self.running[1:], "parents": self.parents, "tokens": self.tokens,
-                "verdict": self.verdict}
 
     def step_out(self, step):
         return {"picks": self.picks[step], "scores": self.scores[step], "n": self.n[step:step + 1],
                 "status": self.status[step:step + 1]}
 
     def read(self, first, last, device):
-        """Host lists of steps [first, last], after one stream synchronisation."""
-        k = last + 1 - first
-        for name, t in self._arrays().items():
-            self.host[name][:k].copy_(t[first:last + 1], non_blocking=True)
-        torch.cuda.current_stream(device).synchronize()
-        return {name: h[:k].tolist() for name, h in self.host.items()}
+        """Host lists of steps [first, last] (running = the scores after each step)."""
+        return _read_block({"picks": self.picks, "scores": self.scores, "n": self.n, "status": self.status,
+                            "running": self.running[1:], "parents": self.parents, "tokens": self.tokens,
+                            "verdict": self.verdict}, first, last, device)
 
 
 def _beam_sample(decoder, embeddings, max_new_tokens, temperature, top_p, beams, stop_ids, eos_id, loop_guard,
@@ -267,12 +273,16 @@ def _beam_sample(decoder, embeddings, max_new_tokens, temperature, top_p, beams,
         raise ValueError(f"stop sequences longer than {_MAX_STOP} tokens are not supported")
     reorder_cache = _device_reorder(decoding, beams)
     every = _SYNC_EVERY if reorder_cache is not None else 1
-    rec = _BeamRecord(steps, beams, keep, every, device)
+    rec = _BeamRecord(steps, beams, keep, device)
     rec.running[0, 1:] = -1e9
     stop_dev = torch.tensor(stop_ids, dtype=torch.int64, device=device) if n_stop else None
     tails = torch.full((2, beams, max(n_stop, 1)), -1, dtype=torch.int64, device=device)
     seen = (ops.seen_bitmap(beams, vocab, device), ops.seen_bitmap(beams, vocab, device))
     hist = torch.zeros((2, beams, steps), dtype=torch.int32, device=device) if loop_guard else None
+    # The incremental loop guard: every running row's window at every step enters
+    # one occurrence table (inside sv_beam_advance); a check probes it for row 0.
+    whash = torch.zeros((2, beams), dtype=torch.int32, device=device) if loop_guard else None
+    table = ops.guard_table(beams * steps, device) if loop_guard else None
     workspace = ops.beam_workspace(beams, vocab, device)
 
     # The reference's host state, with candidates as linked nodes (token, parent).
@@ -337,12 +347,13 @@ def _beam_sample(decoder, embeddings, max_new_tokens, temperature, top_p, beams,
                          tails_in=tails[cur], tails_out=tails[nxt], running_out=rec.running[step + 1],
                          parents_out=rec.parents[step], tokens_out=rec.tokens[step], seen_in=seen[cur],
                          seen_out=seen[nxt], hist_in=None if hist is None else hist[cur],
-                         hist_out=None if hist is None else hist[nxt])
-        if loop_guard and step % 16 == 15 and step + 1 >= LOOP_WINDOW * LOOP_REPEATS:
-            # running[0]'s tokens after this step (runtime_shared.py:254); shorter
-            # histories never repeat (the verdict stays 0).
-            ops.loop_guard(hist[nxt, 0:1, :step + 1], None, LOOP_WINDOW, LOOP_REPEATS,
-                           out=rec.verdict[step:step + 1])
+                         hist_out=None if hist is None else hist[nxt],
+                         whash_in=None if whash is None else whash[cur],
+                         whash_out=None if whash is None else whash[nxt], guard_table=table, window=LOOP_WINDOW)
+        if loop_guard and step % 16 == 15:
+            # running[0]'s tokens after this step (runtime_shared.py:254).
+            ops.loop_guard_incremental(table, hist[nxt, 0], step + 1, step + 1, LOOP_WINDOW, LOOP_REPEATS,
+                                       out=rec.verdict[step:step + 1])
         if step % every == every - 1 or last:
             done, selected = replay(synced, step)
             if done is not None:

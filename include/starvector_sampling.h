@@ -43,6 +43,7 @@ extern "C" {
 #define SV_ST_HISTORY 4    /* a history id outside [0, vocab) */
 #define SV_ST_TIMEOUT 5    /* a bounded wait on an asynchronous copy ran out */
 #define SV_ST_SHARD_OVERFLOW 6 /* sv_merge_shards: a slice's kept list exceeded its capacity */
+#define SV_ST_GUARD_FULL 7     /* sv_loop_guard_incremental: a window did not fit in the table */
 
 /* Logit dtypes. */
 #define SV_F32 0
@@ -309,6 +310,26 @@ int sv_kv_reorder(void* keys, void* values, int32_t elem_bytes, int32_t layers, 
                   int64_t stride_slot, const int64_t* parents, int32_t* out_status, void* stream);
 
 /*
+ * Incremental loop guard (runtime_shared.py:156-167, `_repeating`, checked every 16
+ * steps at :207 and :254) for one growing sequence: the verdict of sv_loop_guard in
+ * time independent of the sequence's length.  `table` (table_entries, a power of
+ * two, 8-byte words; all bits set = empty, fill it with 0xFF before the first call)
+ * holds one entry per (window hash, start) of the sequence's windows.  The call
+ * first inserts the windows ending at positions [insert_from, length) of `tokens`
+ * (int32 or int64, the sequence's first `length` tokens), then counts the starts
+ * whose `window` tokens equal the last `window` (hash matches verified token by
+ * token): out_verdict = length >= window * repeats && count >= repeats.  Calling it
+ * with insert_from = the previous call's length keeps every window in the table.
+ * The beam loop inserts its rows' windows inside sv_beam_advance instead (then
+ * insert_from = length).  Size the table to at least twice the windows inserted;
+ * out_status (may be NULL) gets SV_ST_GUARD_FULL if an insert found no slot.
+ * 1 <= window <= 1024; one CTA.
+ */
+int sv_loop_guard_incremental(unsigned long long* table, int64_t table_entries, const void* tokens,
+                              int32_t token_bytes, int64_t insert_from, int64_t length, int32_t window,
+                              int32_t repeats, uint8_t* out_verdict, int32_t* out_status, void* stream);
+
+/*
  * The beam loop's per-step decision on the device (replaces the host bookkeeping
  * of runtime_shared.py:237-259 that decides the next step; the finished list, stop
  * tests and loop guard stay with the caller).  Inputs are one sv_beam_step's
@@ -326,7 +347,13 @@ int sv_kv_reorder(void* keys, void* values, int32_t elem_bytes, int32_t layers, 
  *                    to skip; packed bitmaps, row stride seen_stride_words),
  *   hist_out[r]    = hist_in[parent][0, step) then the token (optional: both NULL
  *                    to skip; int32 rows of hist_stride > step entries, the running
- *                    rows' generated tokens, for the loop guard).
+ *                    rows' generated tokens, for the loop guard),
+ *   whash_out[r]   = the row's rolling hash of its last `window` tokens (uint32
+ *                    [beams], zero before the first step), its window entered in
+ *                    guard_table once step >= window - 1 (optional: guard_table
+ *                    NULL to skip; needs the histories; the table layout and sizing
+ *                    are sv_loop_guard_incremental's, whose probe with
+ *                    insert_from = length then checks running row 0).
  * A step whose status is non-zero, or without a valid pick, leaves every row its
  * own state (parents r, tokens 0, running 0 / -1e9).  eos_id -1 never matches.
  * beams <= num_picks <= 64, n_stop <= 16; tails_in != tails_out, hist_in != hist_out;
@@ -337,7 +364,8 @@ int sv_beam_advance(const int64_t* picks, const float* pick_scores, const int32_
                     const int64_t* stop_ids, int32_t n_stop, int64_t eos_id, const int64_t* tails_in,
                     int64_t* tails_out, float* running_out, int64_t* parents_out, int64_t* tokens_out,
                     const uint32_t* seen_in, uint32_t* seen_out, int64_t seen_stride_words, const int32_t* hist_in,
-                    int32_t* hist_out, int64_t hist_stride, void* stream);
+                    int32_t* hist_out, int64_t hist_stride, const uint32_t* whash_in, uint32_t* whash_out,
+                    unsigned long long* guard_table, int64_t guard_entries, int32_t window, void* stream);
 
 /* Text of a return or status code. */
 const char* sv_error_string(int32_t code);

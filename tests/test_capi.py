@@ -121,9 +121,11 @@ def test_beam_advance_rejects_invalid_arguments(sv):
     """sv_beam_advance(picks, pick_scores, n_picks, status, beams, vocab, num_picks,
     step, last, stop_ids, n_stop, eos_id, tails_in, tails_out, running_out,
     parents_out, tokens_out, seen_in, seen_out, seen_stride_words, hist_in, hist_out,
-    hist_stride, stream): rejections return before any CUDA call."""
+    hist_stride, whash_in, whash_out, guard_table, guard_entries, window, stream):
+    rejections return before any CUDA call."""
     lib = sv._lib.lib()
-    base = [16, 16, 16, 16, 2, 100, 4, 3, 0, 16, 2, -1, 16, 32, 16, 16, 16, 64, 128, 4, 256, 512, 8, None]
+    base = [16, 16, 16, 16, 2, 100, 4, 3, 0, 16, 2, -1, 16, 32, 16, 16, 16, 64, 128, 4, 256, 512, 8,
+            1024, 1040, 2048, 64, 64, None]
 
     def call(**kw):
         a = list(base)
@@ -139,3 +141,26 @@ def test_beam_advance_rejects_invalid_arguments(sv):
     assert call(a13=16) == -1 and call(a21=256) == -1              # in place
     assert call(a22=3) == -1                                       # history row shorter than step + 1
     assert call(a18=70) == -1                                      # seen_out overlaps seen_in
+    assert call(a20=None, a21=None) == -1                          # the guard needs the histories
+    assert call(a24=1024) == -1 and call(a23=None) == -1           # rolling hashes in place / missing
+    assert call(a26=48) == -3 and call(a27=0) == -3 and call(a27=1025) == -3
+    assert call(a25=2052) == -5                                    # table not 8-byte aligned
+
+
+def test_loop_guard_incremental_rejects_invalid_arguments(sv):
+    """sv_loop_guard_incremental(table, entries, tokens, token_bytes, insert_from,
+    length, window, repeats, out_verdict, out_status, stream)."""
+    lib = sv._lib.lib()
+    base = [64, 1024, 128, 4, 0, 200, 64, 3, 16, None, None]
+
+    def call(**kw):
+        a = list(base)
+        for k, v in kw.items():
+            a[int(k[1:])] = v
+        return lib.sv_loop_guard_incremental(*a)
+
+    assert call(a0=None) == -1 and call(a2=None) == -1 and call(a8=None) == -1
+    assert call(a3=2) == -2
+    assert call(a1=1000) == -3 and call(a1=1) == -3 and call(a4=201) == -3 and call(a5=-1) == -3
+    assert call(a6=0) == -4 and call(a6=1025) == -4 and call(a7=0) == -4
+    assert call(a2=130) == -5 and call(a0=68) == -5

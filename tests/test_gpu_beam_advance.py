@@ -137,3 +137,54 @@ def test_without_optional_state(sv):
                          with_state=False)
     assert out["parents"].tolist() == [0, 1]
     assert out["tokens"].tolist() == [5, 1]
+
+
+@pytest.mark.parametrize("window,repeats", [(8, 3), (64, 3)])
+def test_beam_guard_table_tracks_running_row_0(sv, window, repeats):
+    """A 400-step beam run whose rows are reordered every step: the incremental
+    guard (windows entered by sv_beam_advance, probed for row 0) agrees at every
+    16th step with a full rescan of row 0's history (the oracle)."""
+    from oracle import oracle as O
+    rng = random.Random(window)
+    beams, vocab, steps = 4, 50, 400
+    period = [rng.randrange(vocab) for _ in range(7)]
+    hist = torch.zeros((2, beams, steps), dtype=torch.int32, device=DEV)
+    whash = torch.zeros((2, beams), dtype=torch.int32, device=DEV)
+    table = sv.ops.guard_table(beams * steps, DEV)
+    tails = torch.full((2, beams, 1), -1, dtype=torch.int64, device=DEV)
+    running = torch.zeros((beams,), device=DEV)
+    parents = torch.zeros((beams,), dtype=torch.int64, device=DEV)
+    tokens = torch.zeros((beams,), dtype=torch.int64, device=DEV)
+    verdict = torch.zeros(1, dtype=torch.uint8, device=DEV)
+    checked = hits = 0
+    for step in range(steps):
+        cur, nxt = step % 2, 1 - step % 2
+        flat = []
+        for _ in range(64):  # up to 2 * beams distinct picks (fewer in the periodic stretch)
+            if len(flat) == 2 * beams:
+                break
+            p = rng.randrange(beams)
+            # Periodic in steps [100, 300) (the guard fires there), noisy elsewhere.
+            t = period[step % 7] if 100 <= step < 300 or rng.random() < 0.85 else rng.randrange(vocab)
+            if p * vocab + t not in flat:
+                flat.append(p * vocab + t)
+                if rng.random() < 0.3:
+                    break
+        pad = 2 * beams - len(flat)
+        o = {"picks": torch.tensor(flat + [-1] * pad, dtype=torch.int64, device=DEV),
+             "scores": torch.tensor([rng.uniform(-20, 0) for _ in flat] + [0.0] * pad, dtype=torch.float32,
+                                    device=DEV),
+             "n": torch.tensor([len(flat)], dtype=torch.int32, device=DEV),
+             "status": torch.zeros(1, dtype=torch.int32, device=DEV)}
+        sv.ops.beam_advance(o, beams=beams, vocab=vocab, step=step, last=False, stop_ids=None, eos_id=None,
+                            tails_in=tails[cur], tails_out=tails[nxt], running_out=running, parents_out=parents,
+                            tokens_out=tokens, hist_in=hist[cur], hist_out=hist[nxt], whash_in=whash[cur],
+                            whash_out=whash[nxt], guard_table=table, window=window)
+        if step % 16 == 15:
+            sv.ops.loop_guard_incremental(table, hist[nxt, 0], step + 1, step + 1, window, repeats, out=verdict)
+            row0 = hist[nxt, 0, :step + 1].cpu().numpy()
+            want = bool(O.repeating(row0[None], None, window, repeats)[0])
+            assert bool(verdict.item()) == want, step
+            checked += 1
+            hits += want
+    assert checked == steps // 16 and 0 < hits < checked

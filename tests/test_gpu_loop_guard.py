@@ -61,3 +61,56 @@ def test_all_equal_and_periodic(sv):
     t[2] = np.arange(5000) % 63
     v = sv.loop_guard(torch.from_numpy(t).to(DEV))
     np.testing.assert_array_equal(v.cpu().numpy(), O.repeating(t))
+
+
+def _incremental_verdicts(sv, row, window, repeats, every=16, dtype=torch.int64):
+    """Verdicts of the incremental guard at lengths every, 2*every, ... of one row,
+    entering the new windows at each check."""
+    t = torch.from_numpy(row).to(DEV).to(dtype)
+    table = sv.ops.guard_table(len(row), DEV)
+    out = torch.zeros(len(row) // every, dtype=torch.uint8, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    prev = 0
+    for k, n in enumerate(range(every, len(row) + 1, every)):
+        sv.ops.loop_guard_incremental(table, t, prev, n, window, repeats, out=out[k:k + 1], status=status)
+        prev = n
+    assert int(status) == 0
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("window,repeats", [(1, 3), (8, 2), (64, 3), (64, 5), (200, 3)])
+@pytest.mark.parametrize("dtype", [torch.int32, torch.int64])
+def test_incremental_matches_batched_at_every_check(sv, window, repeats, dtype):
+    """The incremental guard's verdict after each block of 16 tokens equals the
+    full rescan (oracle) of the same prefix: tiny alphabets (many hash-equal
+    windows), planted repeats, periodic and constant stretches."""
+    g = np.random.default_rng(window + repeats)
+    rows = [g.integers(0, 3, 1600), g.integers(0, 40000, 1600), np.ones(1600, np.int64),
+            np.arange(1600) % 37, np.concatenate([g.integers(0, 9, 700), np.tile(g.integers(0, 9, 80), 12)[:900]])]
+    for row in rows:
+        row = row.astype(np.int64)
+        got = _incremental_verdicts(sv, row, window, repeats, dtype=dtype)
+        lengths = np.arange(16, len(row) + 1, 16, dtype=np.int32)
+        want = O.repeating(np.broadcast_to(row.astype(np.int32), (len(lengths), len(row))).copy(), lengths, window,
+                           repeats)
+        np.testing.assert_array_equal(got, want)
+
+
+def test_incremental_built_at_once_on_cfg5(sv):
+    """The whole table entered in one call (insert_from = 0) gives the reference's
+    verdicts on config 5's 16384-token rows."""
+    t, verdict = cfg5_fixture()
+    out = torch.zeros(len(t), dtype=torch.uint8, device=DEV)
+    for r in range(0, len(t), 8):
+        table = sv.ops.guard_table(t.shape[1], DEV)
+        sv.ops.loop_guard_incremental(table, torch.from_numpy(t[r]).to(DEV), 0, t.shape[1], out=out[r:r + 1])
+    np.testing.assert_array_equal(out.cpu().numpy()[::8], verdict[::8])
+
+
+def test_incremental_reports_a_full_table(sv):
+    row = torch.arange(300, dtype=torch.int64, device=DEV)
+    table = torch.full((64,), -1, dtype=torch.int64, device=DEV)  # room for 64 of 237 windows
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    sv.ops.loop_guard_incremental(table, row, 0, 300, out=torch.zeros(1, dtype=torch.uint8, device=DEV),
+                                  status=status)
+    assert int(status) == sv._lib.ST_GUARD_FULL
