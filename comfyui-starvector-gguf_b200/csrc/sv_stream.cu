@@ -68,7 +68,6 @@ struct __align__(128) StreamShared {
   __align__(16) unsigned int bins[SBINS];
   float wsort[NW][32];  // first bound: each warp's values, descending
   int wcount[NW];       // candidates each warp found
-  float boot_kth;       // kk-th largest of the first bound's values
   unsigned int tau_key;   // ordered key of the shared bound (atomicMax)
   unsigned int rmax_key;  // ordered key of the row's largest raw score
   int err;
@@ -542,7 +541,6 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
       sh.err = 0;
       sh.rmax_key = 0;
       sh.tau_key = ord_key(NEG);
-      sh.boot_kth = NEG;
     }
   }
   __syncthreads();
@@ -597,8 +595,9 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
   }
   __syncthreads();
 
-  // 2. the first bound: the kk-th largest of the threads' maxima over the unseen
-  //    elements of the first RING batches (in the order value desc, warp, lane).
+  // 2. the first bound: each thread's maximum over the unseen elements of the
+  //    first RING batches; the smallest of the warps' ceil(kk / warps)-th largest
+  //    maxima (at least kk elements of the row reach it).
   load_batch(w0, 0);
   load_batch(w1, 1);
   load_batch(w2, 2);
@@ -631,24 +630,13 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
     }
     sh.wsort[warp][rank] = g;
     __syncthreads();
+    // Every warp holds jw values >= its jw-th largest: NWARPS * jw >= kk values
+    // reach the smallest of those, a valid first bound.
+    const int jw = (kk + NWARPS - 1) / NWARPS;
+    float b = sh.wsort[0][jw - 1];
 #pragma unroll
-    for (int ow = 0; ow < NWARPS; ++ow) {
-      if (ow == warp) continue;
-      int lo = 0, hi = 32;  // entries of warp ow that come before this value
-#pragma unroll
-      for (int it = 0; it < 6; ++it) {
-        if (lo < hi) {
-          const int mid = (lo + hi) >> 1;
-          const float e = sh.wsort[ow][mid];
-          if (e > g || (e == g && ow < warp)) lo = mid + 1;
-          else hi = mid;
-        }
-      }
-      rank += lo;
-    }
-    if (rank == kk - 1) sh.boot_kth = g;
-    __syncthreads();
-    boot = sh.boot_kth;
+    for (int ow = 1; ow < NWARPS; ++ow) b = fminf(b, sh.wsort[ow][jw - 1]);
+    boot = b;
   }
   float hi_boot = sh.wsort[0][0];
 #pragma unroll
