@@ -141,29 +141,74 @@ int loop_guard_max_window() { return LG_MAXW; }
 
 // ---------------------------------------------------------------------------
 // Incremental loop guard: one sequence's verdict from its window-occurrence table
-// (sv_guard.cuh) in time independent of the sequence's length.  The CTA first
-// inserts the windows ending at positions [from, L) - each thread a contiguous run,
-// the first window hashed directly, the rest rolled - then warp 0 walks the tail
-// hash's probe chain, verifying each candidate start against the tail token by
-// token, until `repeats` distinct starts match (the tail itself among them, as
-// the reference counts it) or an empty slot ends the chain.
+// (sv_guard.cuh) in time independent of the sequence's length.  A check enters
+// the windows ending at positions [from, L) and probes the table for the tail.
+// The latency of a check is a handful of dependent L2 round trips, so each step
+// keeps them few: up to GI_DIRECT new windows (a decode loop enters 16 per check)
+// are staged with the tail in shared memory by one coalesced load and hashed
+// eight lanes per window, all windows at once (each lane sums tok * B^(w-1-k) over
+// its positions k, three shuffles add the group's sums: the hash is a sum mod 2^32,
+// so the order does not matter), then entered together.  More windows (a table
+// built in one call) are hashed by contiguous runs per thread, the first window
+// directly and the rest rolled.  Warp 0 then reads the tail hash's probe chain 32
+// slots per load and verifies each hash match against the tail token by token
+// (the tail's own entry counts without a check), until `repeats` distinct starts
+// match (the tail itself among them, as the reference counts it) or an empty slot
+// ends the chain.
 
 constexpr int GI_NT = 128;
+constexpr int GI_DIRECT = 256;
+
+__device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
 
 template <typename Tok>
 __global__ void __launch_bounds__(GI_NT) guard_incremental_kernel(unsigned long long* table, int64_t mask,
                                                                   const Tok* __restrict__ tokens, int64_t from,
                                                                   int64_t L, int w, int repeats, uint8_t* verdict,
                                                                   int32_t* status) {
-  __shared__ Tok tail[LG_MAXW];
+  __shared__ Tok stage[GI_DIRECT + LG_MAXW];
+  __shared__ uint32_t pw[LG_MAXW];  // B^(w-1-k)
   __shared__ int full;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NWARP = GI_NT / 32;
+  if (L < w) {  // no whole window yet
+    if (tid == 0) {
+      *verdict = 0;
+      if (status) *status = SV_ST_OK;
+    }
+    return;
+  }
   if (tid == 0) full = 0;
-  __syncthreads();
-  const uint32_t bw = guard_pow(kGuardBase, w);
   const int64_t e0 = from > (int64_t)w - 1 ? from : (int64_t)w - 1;
-  if (e0 < L) {
-    const int64_t n = L - e0, per = (n + GI_NT - 1) / GI_NT;
+  const int64_t n = L > e0 ? L - e0 : 0;  // windows to enter
+  const bool direct = n <= GI_DIRECT;
+  // Staged tokens: the windows to enter (direct) and always the tail.
+  const int64_t s0 = (direct && n ? e0 : L - 1) - w + 1;
+  const int slen = (int)(L - s0);
+  for (int j = tid; j < slen; j += GI_NT) stage[j] = tokens[s0 + j];
+  for (int k = tid; k < w; k += GI_NT) pw[k] = guard_pow(kGuardBase, w - 1 - k);
+  __syncthreads();
+  if (direct) {
+    // Eight lanes per window, 16 windows per pass; the loop test is warp-uniform.
+    const int g = lane >> 3, gl = lane & 7;
+    for (int64_t e = e0 + warp * 4 + g; e - g < L; e += NWARP * 4) {
+      const bool act = e < L;
+      uint32_t h = 0;
+      if (act) {
+        const int o = (int)(e - w + 1 - s0);
+        for (int k = gl; k < w; k += 8) h += guard_tok(stage[o + k]) * pw[k];
+      }
+#pragma unroll
+      for (int m = 4; m; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
+      if (act && gl == 0 && !guard_insert(table, mask, h, (uint32_t)(e - w + 1))) full = 1;
+    }
+  } else {
+    const uint32_t bw = guard_pow(kGuardBase, w);
+    const int64_t per = (n + GI_NT - 1) / GI_NT;
     const int64_t a = e0 + tid * per, b = a + per < L ? a + per : L;
     if (a < b) {
       uint32_t h = 0;
@@ -174,23 +219,36 @@ __global__ void __launch_bounds__(GI_NT) guard_incremental_kernel(unsigned long 
       }
     }
   }
-  for (int k = tid; k < w && L >= w; k += GI_NT) tail[k] = tokens[L - w + k];
   __syncthreads();
-  if (tid >= 32) return;
-  const int lane = tid;
+  if (warp != 0) return;
+  const Tok* tail = stage + (slen - w);
   int count = 0;
   if (L >= (int64_t)w * repeats) {
     uint32_t ht = 0;
-    for (int k = 0; k < w; ++k) ht = ht * kGuardBase + guard_tok(tail[k]);
-    int64_t slot = guard_mix(ht) & mask;
-    for (int64_t i = 0; i <= mask && count < repeats; ++i, slot = (slot + 1) & mask) {
-      const unsigned long long e = table[slot];
-      if (e == kGuardEmpty) break;
-      if ((uint32_t)(e >> 32) != ht) continue;
-      const int64_t s = (uint32_t)e;
-      bool eq = s + w <= L;
-      for (int k = lane; k < w && eq; k += 32) eq = tokens[s + k] == tail[k];
-      if (__all_sync(0xffffffffu, eq)) ++count;
+    for (int k = lane; k < w; k += 32) ht += guard_tok(tail[k]) * pw[k];
+    ht = warp_sum_u32(ht);
+    // The entry (ht, L - w) is the tail's own window (every running row's windows
+    // are entered, so it is present): it counts without a check.
+    const uint32_t self = (uint32_t)(L - w);
+    const int64_t slot0 = guard_mix(ht) & mask;
+    for (int64_t i0 = 0; i0 <= mask && count < repeats; i0 += 32) {
+      const unsigned long long e = i0 + lane <= mask ? table[(slot0 + i0 + lane) & mask] : kGuardEmpty;
+      const unsigned empty = __ballot_sync(0xffffffffu, e == kGuardEmpty);
+      const unsigned before = empty ? (1u << (__ffs(empty) - 1)) - 1u : 0xffffffffu;  // the chain's slots
+      unsigned cand = __ballot_sync(0xffffffffu, (uint32_t)(e >> 32) == ht) & before;
+      while (cand && count < repeats) {
+        const int c = __ffs(cand) - 1;
+        cand &= cand - 1;
+        const int64_t s = __shfl_sync(0xffffffffu, (unsigned)(e & 0xffffffffu), c);
+        if (s == self) {
+          ++count;
+          continue;
+        }
+        bool eq = s + w <= L;
+        for (int k = lane; k < w && eq; k += 32) eq = tokens[s + k] == tail[k];
+        if (__all_sync(0xffffffffu, eq)) ++count;
+      }
+      if (empty) break;
     }
   }
   if (lane == 0) {
