@@ -515,12 +515,20 @@ def latency_extras(sv, dev):
     o5 = {}
     sv.sample_step(xs, us_, seen_bits=bits, out=o5)
     out["cfg5_sample_unsharded_us_per_step"] = graph_time_us(lambda: sv.sample_step(xs, us_, seen_bits=bits, out=o5))
+    # Config 5's loop guard: warm (the same 16.8 MB each call, L2-resident) and cold
+    # (ten copies in turn, 168 MB > the 126 MB L2, so each call reads HBM).
     t = torch.from_numpy(cfg5_tokens()).to(dev)
     lens = torch.full((t.shape[0],), t.shape[1], dtype=torch.int32, device=dev)
     v = torch.empty(t.shape[0], dtype=torch.uint8, device=dev)
     sv.loop_guard(t, lens, out=v)
     out["cfg5_loop_guard_us"] = graph_time_us(lambda: sv.loop_guard(t, lens, out=v))
     out["cfg5_loop_guard_GBps"] = t.numel() * 4 / (out["cfg5_loop_guard_us"] * 1e-6) / 1e9
+    copies = [t.clone() for _ in range(10)]
+    turn = iter(range(1 << 30))
+    out["cfg5_loop_guard_cold_us"] = graph_time_us(lambda: sv.loop_guard(copies[next(turn) % 10], lens, out=v),
+                                                   reps=20, per_graph=10)
+    out["cfg5_loop_guard_cold_GBps"] = t.numel() * 4 / (out["cfg5_loop_guard_cold_us"] * 1e-6) / 1e9
+    del copies
     return out
 
 

@@ -2,7 +2,19 @@
 //
 // Verdict for a row of L tokens: L >= window*repeats and the last `window` tokens
 // occur at least `repeats` times (overlapping starts allowed, the tail itself
-// counted).  One CTA per row.  Tokens are staged chunk by chunk in shared memory;
+// counted).
+//
+// Rows with a stride go to loop_guard_scan_kernel: a cluster of P CTAs per row,
+// each streaming its share of the row's window starts in 16-byte vectors (all of
+// a thread's loads of a pass in flight at once) and comparing every start's first
+// token with the tail's first token, the reference's own filter (:163).  The few
+// candidates of a pass are then verified against the whole tail, one warp per
+// candidate, from L2.  The CTAs' counts meet in rank 0 through distributed shared
+// memory.  The work per row is one compare per token plus the verifications, so
+// the kernel runs at the speed of the loads.
+//
+// With row stride 0 (rows given by lengths only) loop_guard_kernel takes the rows:
+// one CTA per row.  Tokens are staged chunk by chunk in shared memory;
 // each thread owns a contiguous run of window starts and rolls a polynomial hash
 // (mod 2^32, odd base, over a 32-bit mix of each token) along it; a start whose
 // hash equals the tail's hash is verified token by token, so the verdict is exact
@@ -10,6 +22,7 @@
 // `repeats` occurrences are found.  A chunk holds 16640 starts, so a 16K-token row
 // is staged once (16-byte vectors when the row is aligned); the rolling step
 // h(s+1) = h(s) B + (x[s+w] - x[s] B^w) keeps one multiply on the dependency chain.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -112,8 +125,133 @@ __global__ void __launch_bounds__(LG_NT) loop_guard_kernel(const Tok* __restrict
 
 size_t loop_guard_smem(int token_bytes) { return (size_t)(LG_CH + 2 * LG_MAXW) * token_bytes; }
 
+namespace cg = cooperative_groups;
+
+constexpr int LS_NT = 256;
+constexpr int LS_U = 4;  // 16-byte vectors per thread per pass
+
+__device__ __forceinline__ void lg_cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+__device__ __forceinline__ void lg_cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+template <typename Tok, int P>
+__global__ void __cluster_dims__(P, 1, 1) __launch_bounds__(LS_NT, sizeof(Tok) == 4 ? 7 : 6)
+    loop_guard_scan_kernel(const Tok* __restrict__ tokens, int64_t stride, const int32_t* __restrict__ lengths,
+                           int w, int repeats, uint8_t* __restrict__ verdict) {
+  constexpr int VE = 16 / (int)sizeof(Tok);
+  constexpr int PASS = LS_NT * LS_U * VE;  // window starts per pass
+  constexpr int NWARP = LS_NT / 32;
+  constexpr unsigned FULL = 0xffffffffu;
+  __shared__ Tok tail[LG_MAXW];
+  __shared__ int cand[PASS];
+  __shared__ int ncand, count, total;  // total: the cluster's count, in rank 0
+  cg::cluster_group cl = cg::this_cluster();
+  const int part = (int)cl.block_rank();
+  const int64_t row = blockIdx.x / P;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const Tok* t = tokens + row * stride;
+  // This CTA's share of the row's possible window starts, from the stride (so the
+  // first loads need not wait for the length): [a, a + per), a a multiple of VE so
+  // that vectors begin on a start.  Loads stay inside the row's stride.
+  const int S = (int)stride;  // < 2^30 (host check): 32-bit positions
+  const int smax = S - w + 1 > 0 ? S - w + 1 : 0;
+  const int per = ((smax + P - 1) / P + VE - 1) / VE * VE;
+  const int a = part * per;
+  const bool vec = (reinterpret_cast<uintptr_t>(t) & 15) == 0;
+  Tok v[LS_U][VE];
+  auto load_pass = [&](int p0, int lim) {
+#pragma unroll
+    for (int u = 0; u < LS_U; ++u) {
+      const int pos = p0 + (u * LS_NT + tid) * VE;
+      if (vec && pos + VE <= lim) {
+        const uint4 q = *reinterpret_cast<const uint4*>(t + pos);
+        memcpy(&v[u][0], &q, 16);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VE; ++j) v[u][j] = pos + j < lim ? t[pos + j] : Tok(0);
+      }
+    }
+  };
+  if (tid == 0) {
+    ncand = 0;
+    count = 0;
+    total = 0;
+  }
+  if (a < smax) load_pass(a, S);
+  int L = lengths[row];
+  // The tail of a full row (the common case), beside the first loads.
+  if (S >= w)
+    for (int k = tid; k < w; k += LS_NT) tail[k] = t[S - w + k];
+  lg_cluster_arrive();  // rank 0's `total` is zero before any CTA adds to it
+  __syncthreads();
+  if (L > S) L = S;
+  if ((int64_t)L < (int64_t)w * repeats) {  // the same for every CTA of the cluster: none waits
+    if (part == 0 && tid == 0) verdict[row] = 0;
+    return;
+  }
+  if (L != S) {
+    for (int k = tid; k < w; k += LS_NT) tail[k] = t[L - w + k];
+    __syncthreads();
+  }
+  const int nst = L - w + 1;  // window starts
+  const int b = a + per < nst ? a + per : nst;
+  const Tok t0 = tail[0];
+  for (int p0 = a; p0 < b; p0 += PASS) {
+#pragma unroll
+    for (int u = 0; u < LS_U; ++u) {
+      const int pos = p0 + (u * LS_NT + tid) * VE;
+#pragma unroll
+      for (int j = 0; j < VE; ++j)
+        if (v[u][j] == t0 && pos + j < b) cand[atomicAdd(&ncand, 1)] = pos + j - p0;
+    }
+    __syncthreads();
+    const int nc = ncand;
+    if (p0 + PASS < b) load_pass(p0 + PASS, L);  // the next pass's loads fly during the checks
+    for (int c = warp; c < nc; c += NWARP) {
+      int done = lane == 0 ? *reinterpret_cast<volatile int*>(&count) >= repeats : 0;
+      if (__shfl_sync(FULL, done, 0)) break;
+      const int st = p0 + cand[c];
+      bool eq = true;
+      for (int k = lane; k < w && eq; k += 32) eq = t[st + k] == tail[k];
+      if (__all_sync(FULL, eq) && lane == 0) atomicAdd(&count, 1);
+    }
+    __syncthreads();
+    if (count >= repeats || p0 + PASS >= b) break;  // read after the barrier: the same in every thread
+    if (tid == 0) ncand = 0;
+    __syncthreads();
+  }
+  lg_cluster_wait();  // every CTA has initialised its `total`
+  if (tid == 0 && count) atomicAdd(cl.map_shared_rank(&total, 0), count);
+  lg_cluster_arrive();  // the adds are done (release) ...
+  lg_cluster_wait();    // ... before rank 0 reads, and rank 0's memory outlives them
+  if (part == 0 && tid == 0) verdict[row] = total >= repeats;
+}
+
+template <typename Tok>
+cudaError_t launch_scan(const Tok* tokens, int rows, int64_t stride, const int32_t* lengths, int window, int repeats,
+                        uint8_t* verdict, cudaStream_t stream) {
+  // CTAs per row: about one pass of window starts each, at most 8 (a portable cluster).
+  constexpr int PASS = LS_NT * LS_U * (16 / (int)sizeof(Tok));
+  const int64_t want = (stride + PASS - 1) / PASS;
+  const int P = want >= 8 ? 8 : want >= 4 ? 4 : want >= 2 ? 2 : 1;
+  const dim3 grid((unsigned)((int64_t)rows * P));
+  switch (P) {
+    case 1: loop_guard_scan_kernel<Tok, 1><<<grid, LS_NT, 0, stream>>>(tokens, stride, lengths, window, repeats, verdict); break;
+    case 2: loop_guard_scan_kernel<Tok, 2><<<grid, LS_NT, 0, stream>>>(tokens, stride, lengths, window, repeats, verdict); break;
+    case 4: loop_guard_scan_kernel<Tok, 4><<<grid, LS_NT, 0, stream>>>(tokens, stride, lengths, window, repeats, verdict); break;
+    default: loop_guard_scan_kernel<Tok, 8><<<grid, LS_NT, 0, stream>>>(tokens, stride, lengths, window, repeats, verdict); break;
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_loop_guard(const void* tokens, int token_bytes, int rows, int64_t stride, const int32_t* lengths,
                               int window, int repeats, uint8_t* verdict, cudaStream_t stream) {
+  if (stride > 0 && stride < (int64_t)1 << 30) {
+    if (token_bytes == 4)
+      return launch_scan(reinterpret_cast<const int32_t*>(tokens), rows, stride, lengths, window, repeats, verdict,
+                         stream);
+    return launch_scan(reinterpret_cast<const int64_t*>(tokens), rows, stride, lengths, window, repeats, verdict,
+                       stream);
+  }
   const size_t smem = loop_guard_smem(token_bytes);
   int dev = 0;
   cudaGetDevice(&dev);

@@ -202,14 +202,16 @@ def loop_guard(tokens, lengths=None, window=64, repeats=3, out=None):
     t = tokens if tokens.dim() == 2 else tokens.unsqueeze(0)
     if t.dtype not in (torch.int32, torch.int64):
         raise ValueError("tokens must be int32 or int64")
-    if t.stride(-1) != 1:
-        t = t.contiguous()
+    if t.stride(-1) != 1 or (t.shape[0] > 1 and t.stride(0) != t.shape[1]):
+        t = t.contiguous()  # the kernel may read each row's whole stride
     R, Lmax = t.shape
     if lengths is None:
         lengths = torch.full((R,), Lmax, dtype=torch.int32, device=t.device)
     ln = lengths.to(device=t.device, dtype=torch.int32).contiguous()
     v = out if out is not None else torch.empty(R, dtype=torch.uint8, device=t.device)
-    rc = L.lib().sv_loop_guard(t.data_ptr(), t.element_size(), R, t.stride(0) if R > 1 else 0, ln.data_ptr(),
+    # A single row passes its own length as the stride (the batched kernel then
+    # splits it across a cluster).
+    rc = L.lib().sv_loop_guard(t.data_ptr(), t.element_size(), R, t.stride(0) if R > 1 else Lmax, ln.data_ptr(),
                                int(window), int(repeats), v.data_ptr(), _stream(t.device))
     L.check(rc, "sv_loop_guard")
     return v.bool() if out is None else v

@@ -168,7 +168,9 @@ int sv_beam_step_noalloc(const void* logits, int32_t logits_dtype, int32_t beams
  * verdict[r] = 1 iff lengths[r] >= window*repeats and the last `window` tokens of
  * row r occur at least `repeats` times.  tokens int32 or int64 (token_bytes 4/8)
  * [rows, row_stride]; 1 <= window <= 1024.  lengths[r] is clamped to row_stride
- * when row_stride > 0 (with row_stride 0 the caller guarantees the length).
+ * when row_stride > 0, and then every row must hold row_stride readable elements
+ * (the kernel may read a row's whole stride before it knows the row's length);
+ * with row_stride 0 the caller guarantees the length.
  */
 int sv_loop_guard(const void* tokens, int32_t token_bytes, int32_t rows, int64_t row_stride, const int32_t* lengths,
                   int32_t window, int32_t repeats, uint8_t* out_verdict, void* stream);
