@@ -19,6 +19,7 @@ DENSE_NONE, DENSE_SCORES, DENSE_PROBS = range(3)
 FLAG_FORCE_GENERAL = 1
 FLAG_CLUSTER = 2
 FLAG_STREAM = 4
+FLAG_TEST_WAIT_TIMEOUT = 8
 
 _P, _I32, _I64, _D, _SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_double, C.c_size_t
 

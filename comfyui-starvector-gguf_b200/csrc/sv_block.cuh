@@ -176,15 +176,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t phase) {
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase: gives up after ~1 s of global time (the
-// timer is read only once the phase is found incomplete).
-__device__ inline bool mbar_wait(void* bar, uint32_t phase) {
+// Bounded wait on an mbarrier phase: gives up after limit_ns of global time, ~1 s
+// by default (the timer is read only once the phase is found incomplete).
+__device__ inline bool mbar_wait(void* bar, uint32_t phase, uint64_t limit_ns = 1000000000ull) {
   const uint32_t b = smem_u32(bar);
   if (mbar_try(b, phase)) return true;
   const uint64_t t0 = gtimer_ns();
   for (;;) {
     if (mbar_try(b, phase)) return true;
-    if (gtimer_ns() - t0 > 1000000000ull) return false;
+    if (gtimer_ns() - t0 > limit_ns) return false;
   }
 }
 

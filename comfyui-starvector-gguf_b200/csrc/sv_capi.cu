@@ -175,6 +175,7 @@ int sv_sample_step(const void* logits, int32_t logits_dtype, int32_t rows, int32
   a.seen_bits = seen_bits_update;
   a.seen_bits_stride = seen_bits_row_stride;
   a.force_slow = (flags & SV_FLAG_FORCE_GENERAL) ? 1 : 0;
+  a.wait_test = (flags & SV_FLAG_TEST_WAIT_TIMEOUT) ? 1 : 0;
   // Path: the streaming kernel for many rows when the row's seen mask fits a CTA.
   const size_t ssmem = stream_smem_bytes(vocab);
   bool use_stream = ssmem > 0 && rows >= stream_min_rows();

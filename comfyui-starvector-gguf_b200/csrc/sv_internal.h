@@ -65,6 +65,7 @@ struct RowArgs {
   int64_t ws_cap;  // kept entries per beam in the workspace (= vocab)
   // layout
   int32_t S, slice_len, force_slow;
+  int32_t wait_test;  // SV_FLAG_TEST_WAIT_TIMEOUT: the history wait runs out (test hook)
   uint32_t region_a;  // bytes of the per-CTA union region
 };
 

@@ -526,7 +526,8 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
     mbar_init(&sh.idbar, 1);
     fence_proxy_async_smem();  // the initialised barrier is visible to the bulk copy
     if (tma_bytes) {
-      mbar_expect_tx(&sh.idbar, tma_bytes);
+      // The test hook expects 16 bytes the copy never brings: the wait runs out.
+      mbar_expect_tx(&sh.idbar, tma_bytes + (a.wait_test ? 16u : 0u));
       bulk_g2s(sh.stage, hrow, tma_bytes, &sh.idbar);
     }
   }
@@ -555,9 +556,10 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
         else atomicOr(&bits[x >> 5], 1u << (x & 31));
       }
       if (tma_bytes) {
-        if (!__all_sync(FULL, mbar_wait(&sh.idbar, 0))) {  // warp-uniform, for the reductions below
+        const uint64_t limit = a.wait_test ? 2000000ull : 1000000000ull;
+        if (!__all_sync(FULL, mbar_wait(&sh.idbar, 0, limit))) {  // warp-uniform, for the reductions below
           e |= 1 << ST_TIMEOUT;
-          (void)mbar_wait(&sh.idbar, 0);  // let a late copy land before the region is reused
+          (void)mbar_wait(&sh.idbar, 0, limit);  // let a late copy land before the region is reused
         } else {
           const uint4* st = reinterpret_cast<const uint4*>(sh.stage);
           const int nvec = (int)(tma_bytes >> 4);

@@ -82,7 +82,8 @@ def seen_bitmap(rows, vocab, device):
 
 def sample_step(logits, uniforms, *, history=None, history_len=None, seen=None, seen_bits=None,
                 temperature=1.5, top_p=0.9, top_k=50, keep=1, repetition_penalty=3.1, out_capacity=0,
-                dense=None, update_seen_bits=None, force_general=False, path=None, out=None):
+                dense=None, update_seen_bits=None, force_general=False, path=None, out=None,
+                test_wait_timeout=False):
     """Fused penalty + temperature + top-k + top-p + softmax + draw for each row.
 
     Mirrors runtime_shared.py:200-202 per row (see include/starvector_sampling.h).
@@ -90,6 +91,8 @@ def sample_step(logits, uniforms, *, history=None, history_len=None, seen=None, 
     requested idx/prob/score [R, out_capacity] (kept tokens in index order) and
     dense [R, V] ('scores' = the _warp output, 'probs' = its softmax).
     path: None (automatic), 'stream' or 'cluster' selects the kernel.
+    test_wait_timeout: test hook (SV_FLAG_TEST_WAIT_TIMEOUT): the streaming kernel's
+    history-copy wait runs out and the rows report SV_ST_TIMEOUT.
     """
     x = _rows(logits)
     R, V = x.shape
@@ -122,8 +125,8 @@ def sample_step(logits, uniforms, *, history=None, history_len=None, seen=None, 
         o["token"].data_ptr(), o["count"].data_ptr(), _ptr(o.get("idx")), _ptr(o.get("prob")), _ptr(o.get("score")),
         int(out_capacity), _ptr(o.get("dense")), mode, V, o["status"].data_ptr(),
         _ptr(upd), 0 if upd is None else (upd.stride(0) if upd.dim() == 2 else upd.shape[-1]),
-        (L.FLAG_FORCE_GENERAL if force_general else 0) | {None: 0, "cluster": L.FLAG_CLUSTER,
-                                                          "stream": L.FLAG_STREAM}[path], _stream(dev))
+        (L.FLAG_FORCE_GENERAL if force_general else 0) | (L.FLAG_TEST_WAIT_TIMEOUT if test_wait_timeout else 0)
+        | {None: 0, "cluster": L.FLAG_CLUSTER, "stream": L.FLAG_STREAM}[path], _stream(dev))
     L.check(rc, "sv_sample_step")
     return o
 

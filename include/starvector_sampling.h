@@ -66,6 +66,10 @@ extern "C" {
 #define SV_FLAG_FORCE_GENERAL 1 /* take the general (tie-group) path for every row */
 #define SV_FLAG_CLUSTER 2       /* sv_sample_step: use the cluster kernel (rows split across CTAs) */
 #define SV_FLAG_STREAM 4        /* sv_sample_step: use the streaming kernel (one CTA per row) */
+#define SV_FLAG_TEST_WAIT_TIMEOUT 8 /* test hook (sv_sample_step, streaming kernel, id histories staged by
+                                       bulk copy): the history copy's barrier expects 16 bytes more than
+                                       the copy brings, so its bounded wait runs out after ~2 ms and every
+                                       such row reports SV_ST_TIMEOUT; the copy itself lands */
 
 /*
  * One sample-mode step for `rows` independent sequences.

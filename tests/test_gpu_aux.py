@@ -1,6 +1,8 @@
 """GPU parity of the drop-in's element-wise helpers against the reference's rules,
 through the C ABI: the penalty alone (sv_penalize, runtime_shared.py:170-173) and
-the beam step's seen-mask reorder (sv_seen_reorder, runtime_shared.py:258-259)."""
+the beam step's seen-mask reorder (sv_seen_reorder, runtime_shared.py:258-259); and
+the batched kernel's bounded wait running out (SV_ST_TIMEOUT) without losing the
+context."""
 import numpy as np
 import pytest
 import torch
@@ -73,3 +75,26 @@ def test_seen_reorder_matches_reference_rule(sv, beams, vocab):
         got = np.unpackbits(dst.cpu().numpy().view(np.uint8), axis=1, bitorder="little")
         np.testing.assert_array_equal(got[:, :vocab].astype(bool), ref.numpy())
         assert not got[:, vocab:words * 32].any()  # padding bits stay clear
+
+
+def test_history_wait_timeout_reports_status_and_context_survives(sv):
+    """The bounded wait on the history copy (SV_ST_TIMEOUT): the test hook makes the
+    copy's barrier expect 16 bytes the copy never brings, so the wait runs out (after
+    ~2 ms instead of ~1 s); every row reports status 5 and token -1, and the next,
+    normal call on the same context gives the oracle's tokens."""
+    import bench
+    from oracle import oracle as O
+    d = bench.cfg4(seed=5, rows=8, vocab=4096, hist_len=512)
+    x = torch.from_numpy(d["logits"]).cuda()
+    h = torch.from_numpy(d["history"]).cuda()
+    u = torch.from_numpy(d["uniforms"]).cuda()
+    for _ in range(2):
+        o = sv.sample_step(x, u, history=h, path="stream", test_wait_timeout=True)
+        torch.cuda.synchronize()
+        assert o["status"].tolist() == [sv._lib.ST_TIMEOUT] * 8
+        assert o["token"].tolist() == [-1] * 8
+    o = sv.sample_step(x, u, history=h, path="stream")
+    lengths = np.full(8, d["history"].shape[1], np.int32)
+    want = O.sample(d["logits"], d["uniforms"], ids=d["history"], lengths=lengths, temperature=1.5, top_p=0.9)
+    assert o["status"].tolist() == [0] * 8
+    np.testing.assert_array_equal(o["token"].cpu().numpy(), want["token"])
