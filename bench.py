@@ -497,6 +497,19 @@ def latency_extras(sv, dev):
     o1 = {}
     sv.sample_step(x, u, history=h, out=o1, dense="probs")
     out["cfg1_us_per_step"] = graph_time_us(lambda: sv.sample_step(x, u, history=h, out=o1, dense="probs"))
+    # The same step called eagerly through the Python wrapper and the torch extension:
+    # host time per call (submission only) and wall time per call (max of host and GPU).
+    import time
+    n = 500
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(n):
+        sv.sample_step(x, u, history=h, out=o1, dense="probs")
+    t1 = time.perf_counter()
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    out["cfg1_eager_host_us_per_call"] = (t1 - t0) / n * 1e6
+    out["cfg1_eager_wall_us_per_call"] = (t2 - t0) / n * 1e6
     for name, gen, dt in (("cfg2_beam2_us_per_step", cfg2, torch.float32),
                           ("cfg3_beam8_bf16_us_per_step", cfg3, torch.bfloat16)):
         d = gen()

@@ -2,7 +2,10 @@
 
 Every function enqueues on the current CUDA stream of the tensors' device and does
 not synchronise; results are device tensors.  Inputs must be CUDA tensors: there is
-no CPU path.
+no CPU path.  The hot entry points (sample_step, beam_step, beam_advance,
+kv_reorder, loop_guard, loop_guard_incremental) go through the thin PyTorch
+extension sv_torch (ext/sv_torch.cpp), the others through ctypes (_lib.py); both
+call the same C library.
 """
 from __future__ import annotations
 
@@ -39,8 +42,31 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+_EXT = []
+
+
+def _ext():
+    """The thin PyTorch extension (sv_torch, built beside the C-ABI library by
+    build.py): the hot entry points take tensors through it.  Raises if it is
+    missing; there is no other path."""
+    if not _EXT:
+        import importlib
+        try:
+            _EXT.append(importlib.import_module(__package__ + ".sv_torch"))
+        except ImportError as e:
+            raise RuntimeError("the sv_torch extension is not built (run comfyui-starvector-gguf_b200/build.py)") \
+                from e
+    return _EXT[0]
+
+
 def _history(rows, vocab, history=None, history_len=None, seen=None, seen_bits=None):
     """(pointer, kind, row stride, len pointer, cols, keep-alive) for one history form."""
+    t, kind, stride, lens, cols = _history_t(rows, vocab, history, history_len, seen, seen_bits)
+    return _ptr(t), kind, stride, _ptr(lens), cols, (t, lens)
+
+
+def _history_t(rows, vocab, history=None, history_len=None, seen=None, seen_bits=None):
+    """(tensor, kind, row stride, lengths tensor, cols) for one history form."""
     if sum(x is not None for x in (history, seen, seen_bits)) > 1:
         raise ValueError("pass at most one of history, seen, seen_bits")
     if history is not None:
@@ -55,7 +81,7 @@ def _history(rows, vocab, history=None, history_len=None, seen=None, seen_bits=N
         lens = None
         if history_len is not None:
             lens = history_len.to(device=h.device, dtype=torch.int32).contiguous()
-        return h.data_ptr(), kind, stride, _ptr(lens), h.shape[1], (h, lens)
+        return h, kind, stride, lens, h.shape[1]
     if seen is not None:
         _need_cuda(seen, "seen")
         s = seen if seen.dim() == 2 else seen.unsqueeze(0)
@@ -64,15 +90,15 @@ def _history(rows, vocab, history=None, history_len=None, seen=None, seen_bits=N
         if s.stride(-1) != 1:
             s = s.contiguous()
         stride = s.stride(0) if s.shape[0] > 1 else 0
-        return s.data_ptr(), L.HIST_MASK8, stride, None, 0, (s,)
+        return s, L.HIST_MASK8, stride, None, 0
     if seen_bits is not None:
         _need_cuda(seen_bits, "seen_bits")
         b = seen_bits if seen_bits.dim() == 2 else seen_bits.unsqueeze(0)
         if b.dtype != torch.int32 or b.stride(-1) != 1:
             raise ValueError("seen_bits must be a contiguous int32 bitmap [rows, ceil(vocab/32)]")
         stride = b.stride(0) if b.shape[0] > 1 else 0
-        return b.data_ptr(), L.HIST_BITS32, stride, None, 0, (b,)
-    return None, L.HIST_NONE, 0, None, 0, ()
+        return b, L.HIST_BITS32, stride, None, 0
+    return None, L.HIST_NONE, 0, None, 0
 
 
 def seen_bitmap(rows, vocab, device):
@@ -101,7 +127,7 @@ def sample_step(logits, uniforms, *, history=None, history_len=None, seen=None, 
     u = uniforms.reshape(-1)
     if u.dtype != torch.float32 or not u.is_contiguous() or u.numel() < R:
         raise ValueError("uniforms must be a contiguous float32 tensor with one value per row")
-    hp, hk, hs, hl, hc, _keep = _history(R, V, history, history_len, seen, seen_bits)
+    ht, hk, hs, hl, hc = _history_t(R, V, history, history_len, seen, seen_bits)
     o = out if out is not None else {}  # filled in place: callers may preallocate
     if "token" not in o:
         o["token"] = torch.empty(R, dtype=torch.int64, device=dev)
@@ -119,14 +145,13 @@ def sample_step(logits, uniforms, *, history=None, history_len=None, seen=None, 
     upd = update_seen_bits
     if upd is not None:
         _need_cuda(upd, "update_seen_bits")
-    rc = L.lib().sv_sample_step(
-        x.data_ptr(), _DTYPES[x.dtype], R, V, x.stride(0) if R > 1 else 0, hp, hk, hs, hl, hc, u.data_ptr(),
-        float(temperature), float(top_p), int(top_k), int(keep), float(repetition_penalty),
-        o["token"].data_ptr(), o["count"].data_ptr(), _ptr(o.get("idx")), _ptr(o.get("prob")), _ptr(o.get("score")),
-        int(out_capacity), _ptr(o.get("dense")), mode, V, o["status"].data_ptr(),
-        _ptr(upd), 0 if upd is None else (upd.stride(0) if upd.dim() == 2 else upd.shape[-1]),
+    rc = _ext().sample_step(
+        x, R, V, x.stride(0) if R > 1 else 0, ht, hk, hs, hl, hc, u, float(temperature), float(top_p), int(top_k),
+        int(keep), float(repetition_penalty), o["token"], o["count"], o.get("idx"), o.get("prob"), o.get("score"),
+        int(out_capacity), o.get("dense"), mode, V, o["status"],
+        upd, 0 if upd is None else (upd.stride(0) if upd.dim() == 2 else upd.shape[-1]),
         (L.FLAG_FORCE_GENERAL if force_general else 0) | (L.FLAG_TEST_WAIT_TIMEOUT if test_wait_timeout else 0)
-        | {None: 0, "cluster": L.FLAG_CLUSTER, "stream": L.FLAG_STREAM}[path], _stream(dev))
+        | {None: 0, "cluster": L.FLAG_CLUSTER, "stream": L.FLAG_STREAM}[path])
     L.check(rc, "sv_sample_step")
     return o
 
@@ -170,7 +195,7 @@ def beam_step(logits, running_scores, uniforms, *, history=None, history_len=Non
     _need_cuda(u, "uniforms")
     if u.dtype != torch.float32 or not u.is_contiguous() or u.numel() < P:
         raise ValueError("uniforms must be a contiguous float32 tensor with num_picks values")
-    hp, hk, hs, hl, hc, _keep = _history(B, V, history, history_len, seen, seen_bits)
+    ht, hk, hs, hl, hc = _history_t(B, V, history, history_len, seen, seen_bits)
     o = out if out is not None else {}  # filled in place: callers may preallocate
     # Only missing outputs are allocated (a preallocated dict costs no kernels).
     need = {"picks": lambda: torch.full((P,), -1, dtype=torch.int64, device=dev),
@@ -188,13 +213,11 @@ def beam_step(logits, running_scores, uniforms, *, history=None, history_len=Non
         if k not in o:
             o[k] = make()
     ws = workspace if workspace is not None else beam_workspace(B, V, dev)
-    rc = L.lib().sv_beam_step(
-        x.data_ptr(), _DTYPES[x.dtype], B, V, x.stride(0) if B > 1 else 0, hp, hk, hs, hl, hc, rs.data_ptr(),
-        u.data_ptr(), P, float(temperature), float(top_p), int(top_k), int(keep), float(repetition_penalty),
-        o["picks"].data_ptr(), o["scores"].data_ptr(), o["n"].data_ptr(), o["status"].data_ptr(),
-        _ptr(o.get("kept_count")), _ptr(o.get("kept_idx")), _ptr(o.get("kept_logprob")), _ptr(o.get("kept_prob")),
-        int(out_capacity), _ptr(o.get("dense_logprob")), V, ws.data_ptr(), ws.numel(),
-        L.FLAG_FORCE_GENERAL if force_general else 0, _stream(dev))
+    rc = _ext().beam_step(
+        x, B, V, x.stride(0) if B > 1 else 0, ht, hk, hs, hl, hc, rs, u, P, float(temperature), float(top_p),
+        int(top_k), int(keep), float(repetition_penalty), o["picks"], o["scores"], o["n"], o["status"],
+        o.get("kept_count"), o.get("kept_idx"), o.get("kept_logprob"), o.get("kept_prob"), int(out_capacity),
+        o.get("dense_logprob"), V, ws, L.FLAG_FORCE_GENERAL if force_general else 0)
     L.check(rc, "sv_beam_step")
     return o
 
@@ -214,8 +237,7 @@ def loop_guard(tokens, lengths=None, window=64, repeats=3, out=None):
     v = out if out is not None else torch.empty(R, dtype=torch.uint8, device=t.device)
     # A single row passes its own length as the stride (the batched kernel then
     # splits it across a cluster).
-    rc = L.lib().sv_loop_guard(t.data_ptr(), t.element_size(), R, t.stride(0) if R > 1 else Lmax, ln.data_ptr(),
-                               int(window), int(repeats), v.data_ptr(), _stream(t.device))
+    rc = _ext().loop_guard(t, R, t.stride(0) if R > 1 else Lmax, ln, int(window), int(repeats), v)
     L.check(rc, "sv_loop_guard")
     return v.bool() if out is None else v
 
@@ -266,14 +288,12 @@ def beam_advance(step_out, *, beams, vocab, step, last, stop_ids, eos_id, tails_
     _need_cuda(picks, "picks")
     S = stop_ids.numel() if stop_ids is not None else 0
     words = (int(vocab) + 31) // 32
-    rc = L.lib().sv_beam_advance(
-        picks.data_ptr(), scores.data_ptr(), step_out["n"].data_ptr(), step_out["status"].data_ptr(), int(beams),
-        int(vocab), picks.numel(), int(step), int(bool(last)), _ptr(stop_ids) if S else None, S,
-        -1 if eos_id is None else int(eos_id), _ptr(tails_in) if S else None, _ptr(tails_out) if S else None,
-        running_out.data_ptr(), parents_out.data_ptr(), tokens_out.data_ptr(), _ptr(seen_in), _ptr(seen_out),
-        seen_in.stride(0) if seen_in is not None else words, _ptr(hist_in), _ptr(hist_out),
-        hist_in.stride(0) if hist_in is not None else 0, _ptr(whash_in), _ptr(whash_out), _ptr(guard_table),
-        0 if guard_table is None else guard_table.numel(), int(window), _stream(picks.device))
+    rc = _ext().beam_advance(
+        picks, scores, step_out["n"], step_out["status"], int(beams), int(vocab), int(step), bool(last),
+        stop_ids if S else None, -1 if eos_id is None else int(eos_id), tails_in if S else None,
+        tails_out if S else None, running_out, parents_out, tokens_out, seen_in, seen_out,
+        seen_in.stride(0) if seen_in is not None else words, hist_in, hist_out,
+        hist_in.stride(0) if hist_in is not None else 0, whash_in, whash_out, guard_table, int(window))
     L.check(rc, "sv_beam_advance")
 
 
@@ -300,9 +320,8 @@ def loop_guard_incremental(table, tokens, insert_from, length, window=64, repeat
     if table.dtype != torch.int64 or not table.is_contiguous():
         raise ValueError("table must be a contiguous int64 tensor (guard_table)")
     v = out if out is not None else torch.empty(1, dtype=torch.uint8, device=t.device)
-    rc = L.lib().sv_loop_guard_incremental(table.data_ptr(), table.numel(), t.data_ptr(), t.element_size(),
-                                           int(insert_from), int(length), int(window), int(repeats), v.data_ptr(),
-                                           _ptr(status), _stream(t.device))
+    rc = _ext().loop_guard_incremental(table, t, int(insert_from), int(length), int(window), int(repeats), v,
+                                       status)
     L.check(rc, "sv_loop_guard_incremental")
     return v
 
@@ -534,6 +553,5 @@ def kv_reorder(keys, values, parents, length, out_status=None):
     _need_cuda(p, "parents")
     if p.dtype != torch.int64 or not p.is_contiguous() or p.numel() != B:
         raise ValueError("parents must be a contiguous int64 tensor [beams]")
-    rc = L.lib().sv_kv_reorder(keys.data_ptr(), _ptr(values), keys.element_size(), Lr, B, H, int(length), D, sl, sb,
-                               sh, ss, p.data_ptr(), _ptr(out_status), _stream(keys.device))
+    rc = _ext().kv_reorder(keys, values, Lr, B, H, int(length), D, sl, sb, sh, ss, p, out_status)
     L.check(rc, "sv_kv_reorder")

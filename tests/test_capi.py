@@ -164,3 +164,21 @@ def test_loop_guard_incremental_rejects_invalid_arguments(sv):
     assert call(a1=1000) == -3 and call(a1=1) == -3 and call(a4=201) == -3 and call(a5=-1) == -3
     assert call(a6=0) == -4 and call(a6=1025) == -4 and call(a7=0) == -4
     assert call(a2=130) == -5 and call(a0=68) == -5
+
+
+def test_torch_extension_loads_and_checks_tensors(sv):
+    """The thin PyTorch extension (sv_torch) loads beside the C library and rejects
+    non-CUDA tensors with a clear error before any CUDA call."""
+    import torch
+    ext = sv.ops._ext()
+    assert ext.abi_version() == sv._lib.lib().sv_abi_version()
+    for name in ("sample_step", "beam_step", "beam_advance", "kv_reorder", "loop_guard", "loop_guard_incremental"):
+        assert callable(getattr(ext, name))
+    x = torch.zeros(2, 64)
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        ext.loop_guard(torch.zeros(2, 64, dtype=torch.int32), 2, 64, torch.zeros(2, dtype=torch.int32), 8, 3,
+                       torch.zeros(2, dtype=torch.uint8))
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        ext.sample_step(x, 2, 64, 64, None, 0, 0, None, 0, torch.zeros(2), 1.5, 0.9, 50, 1, 3.1,
+                        torch.zeros(2, dtype=torch.int64), None, None, None, None, 0, None, 0, 64,
+                        torch.zeros(2, dtype=torch.int32), None, 0, 0)
