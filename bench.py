@@ -431,6 +431,7 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and not args.no_extras:
         extras.update(kv_extras(sv, dev))
         extras.update(guard_extras(sv, dev))
+        extras.update(advance_extras(sv, dev))
         extras.update(dropin_extras(sv, dev))
     if world > 1 and not args.no_extras:
         extras.update(vocab_sharded_extra(sv, dev, rank, world))  # every rank takes part
@@ -596,6 +597,40 @@ def guard_extras(sv, dev):
         v = torch.zeros(1, dtype=torch.uint8, device=dev)
         out[f"loop_guard_rescan_{n}_us"] = graph_time_us(lambda: sv.loop_guard(t[None], lens, out=v), reps=20,
                                                          per_graph=10)
+    return out
+
+
+def advance_extras(sv, dev):
+    """The beam loop's per-step decision kernel (sv_beam_advance) at V=49152, step
+    1000 of a generation: the decision, the seen-bitmap and history reorder and the
+    loop-guard insert, for 2 and 8 beams."""
+    import torch
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(5)
+    for beams in (2, 8):
+        P, step, words = 2 * beams, 1000, (V + 31) // 32
+        o = {"picks": torch.randperm(beams * V, generator=g, device=dev)[:P].contiguous(),
+             "scores": -torch.rand(P, generator=g, device=dev) * 50, "n": torch.full((1,), P, dtype=torch.int32,
+                                                                                     device=dev),
+             "status": torch.zeros(1, dtype=torch.int32, device=dev)}
+        stop = torch.tensor([5, 6], dtype=torch.int64, device=dev)
+        tails = torch.full((2, beams, 2), -1, dtype=torch.int64, device=dev)
+        seen = torch.zeros((2, beams, words), dtype=torch.int32, device=dev)
+        hist = torch.zeros((2, beams, 4096), dtype=torch.int32, device=dev)
+        whash = torch.zeros((2, beams), dtype=torch.int32, device=dev)
+        table = sv.ops.guard_table(beams * 4096, dev)
+        run = torch.zeros(beams, device=dev)
+        par = torch.zeros(beams, dtype=torch.int64, device=dev)
+        tok = torch.zeros(beams, dtype=torch.int64, device=dev)
+
+        def call():
+            sv.ops.beam_advance(o, beams=beams, vocab=V, step=step, last=False, stop_ids=stop, eos_id=7,
+                                tails_in=tails[0], tails_out=tails[1], running_out=run, parents_out=par,
+                                tokens_out=tok, seen_in=seen[0], seen_out=seen[1], hist_in=hist[0],
+                                hist_out=hist[1], whash_in=whash[0], whash_out=whash[1], guard_table=table,
+                                window=64)
+        call()
+        out[f"beam_advance_{beams}_us"] = graph_time_us(call, reps=20, per_graph=10)
     return out
 
 

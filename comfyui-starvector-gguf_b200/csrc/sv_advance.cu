@@ -227,11 +227,12 @@ extern "C" int sv_beam_advance(const int64_t* picks, const float* pick_scores, c
   a.guard_table = guard_table;
   a.guard_mask = guard_entries - 1;
   a.window = window;
-  // One block per 4096 copied words (every block repeats the small decision).
+  // One block per ANT copied words, so each thread moves one word in one round trip
+  // (every block repeats the small decision, which is cheaper than a second pass).
   const int64_t items = (seen_in ? (int64_t)beams * words : 0) + (hist_in ? (int64_t)beams * (step + 1) : 0);
-  int64_t blocks = (items + 4095) / 4096;
+  int64_t blocks = (items + ANT - 1) / ANT;
   if (blocks < 1) blocks = 1;
-  if (blocks > 148) blocks = 148;
+  if (blocks > 148 * 8) blocks = 148 * 8;
   beam_advance_kernel<<<(unsigned)blocks, ANT, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return cudaGetLastError() == cudaSuccess ? SV_OK : SV_E_CUDA;
 }
