@@ -849,4 +849,127 @@ __device__ Kept leader_slow(const RowArgs& a, BlockScratch<NT>& bs, unsigned cha
   return k;
 }
 
+// ------------------------------------------------- small-candidate finish
+
+// Shared state of finish_small (the batched kernel lays it over its hit queues,
+// which are dead by then; the vocab-sharded merge over its sorted list).
+struct SmallFin {
+  ulonglong2 kw[64];   // candidates: {(value key, index), weight}
+  ulonglong2 kw2[64];  // kept entries: {index, weight}
+  unsigned long long all, below, removed;
+  float thr;
+  int f0, r, hit, last;
+};
+
+// The finish of a row with m <= 64 candidates (fv, fi: tempered scores and
+// indices) by the whole block, two threads per candidate: each pair finds its
+// candidate's position and inclusive prefix sum in the ascending (value, index)
+// order, then in the index order of the kept entries, each thread taking every
+// other candidate and the pair adding their halves with one shuffle.  The k-th
+// largest with ties (runtime_shared.py:180-181), top-p with `keep` (:182-186) and
+// the index-order draw use the same exact integer arithmetic as warp_finish and
+// leader_fast.  M is the largest candidate.  Returns the Kept summary, sets
+// *token and writes the kept list in index order to kidx / kval (which may alias
+// fi / fv).  Every thread of the block must call it.
+template <int NT>
+__device__ Kept finish_small(const RowArgs& a, const float* fv, const int* fi, int m, float M, float u,
+                             int64_t* token, int* kidx, float* kval, SmallFin& f) {
+  static_assert(NT >= 128, "two threads per candidate, 64 candidates");
+  constexpr unsigned FULL = 0xffffffffu;
+  const int tid = threadIdx.x;
+  const int j = tid >> 1, h = tid & 1;
+  const bool act = j < m;
+  const float NEG = Elem<float>::neg_inf();
+  float v = NEG;
+  int id = 0;
+  uint64_t key = ~0ull, e = 0;
+  if (act) {
+    v = fv[j];
+    id = fi[j];
+    key = ((uint64_t)ord_key(v) << 32) | (uint32_t)id;
+    e = fixw(sv_exp(__fsub_rn(v, M)));
+    if (h == 0) f.kw[j] = make_ulonglong2(key, e);
+  }
+  if (tid == 0) {
+    f.below = 0;
+    f.removed = 0;
+    f.thr = NEG;
+    f.f0 = 0;
+    f.r = 0;
+    f.hit = 0x7fffffff;
+    f.last = -1;
+  }
+  __syncthreads();
+  // Position and inclusive prefix sum in the ascending (value, index) order.
+  int rk = 0;
+  uint64_t S = 0;
+  if (act) {
+#pragma unroll 4
+    for (int i = h; i < m; i += 2) {
+      const ulonglong2 kw = f.kw[i];
+      rk += kw.x < key;
+      S += kw.x <= key ? kw.y : 0ull;
+    }
+  }
+  rk += __shfl_xor_sync(FULL, rk, 1);
+  S += __shfl_xor_sync(FULL, S, 1);
+  if (act && h == 0) {
+    if (m >= a.kk && rk == m - a.kk) f.thr = v;  // the k-th largest value
+    if (rk == m - 1) f.all = S;                  // the largest holds the whole mass
+  }
+  __syncthreads();
+  const float thr = f.thr;
+  const bool in = act && v >= thr;  // ties with the k-th largest are kept
+  if (act && h == 0 && !in) {
+    atomicAdd(&f.f0, 1);
+    atomicAdd(&f.below, (unsigned long long)e);
+  }
+  __syncthreads();
+  const int f0 = f.f0, m1 = m - f0;
+  const uint64_t below = f.below, total = f.all - below;
+  // Top-p: the ascending prefix with mass <= floor(total * pthr) goes, never the
+  // last `keep`.
+  bool rm = false;
+  if (a.pthr > 0.0f && in) {
+    const uint64_t thrW = mulfloor(total, a.pthr);
+    const int cap = m1 - a.keep > 0 ? m1 - a.keep : 0;
+    rm = S - below <= thrW && rk - f0 < cap;
+    if (rm && h == 0) {
+      atomicAdd(&f.r, 1);
+      atomicMax(&f.removed, (unsigned long long)(S - below));
+    }
+  }
+  const bool q = in && !rm;
+  if (act && h == 0) f.kw2[j] = make_ulonglong2(q ? (uint64_t)(uint32_t)id : ~0ull, q ? e : 0ull);
+  __syncthreads();
+  Kept kp;
+  kp.n = m1 - f.r;
+  kp.M = M;
+  kp.tot = total - f.removed;
+  // Position and inclusive prefix sum in index order over the kept entries; the
+  // draw is the first index whose prefix exceeds floor(u * mass), else the last.
+  int p = 0;
+  uint64_t Q = 0;
+  if (act) {
+    const uint64_t ix = (uint32_t)id;
+#pragma unroll 4
+    for (int i = h; i < m; i += 2) {
+      const ulonglong2 kw = f.kw2[i];
+      p += kw.x < ix;
+      Q += kw.x <= ix ? kw.y : 0ull;
+    }
+  }
+  p += __shfl_xor_sync(FULL, p, 1);
+  Q += __shfl_xor_sync(FULL, Q, 1);
+  if (q && h == 0) {
+    if (Q > mulfloor(kp.tot, u)) atomicMin(&f.hit, id);
+    atomicMax(&f.last, id);
+    kidx[p] = id;
+    kval[p] = v;
+  }
+  __syncthreads();
+  *token = f.hit != 0x7fffffff ? f.hit : f.last;
+  return kp;
+}
+
 }  // namespace sv

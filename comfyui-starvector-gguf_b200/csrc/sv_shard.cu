@@ -64,6 +64,7 @@ struct MergeArgs {
 struct __align__(16) MergeShared {
   BlockScratch<MNT> bs;
   int n, err, overflow;
+  float wmx[MNT / 32];  // warps' largest candidates (the small finish's M)
   __align__(16) float cv[kMergeMax];  // union; then leader_fast's P / the kept list
   int ci[kMergeMax];
   __align__(16) float fv[kMergeMax];  // candidates >= the k-th largest; then W
@@ -77,45 +78,71 @@ __global__ void __launch_bounds__(MNT) merge_kernel(const MergeArgs m, const Row
   const int row = blockIdx.x, tid = threadIdx.x;
   const int rec = 2 * m.cap + 2;
   if (tid == 0) {
-    sh.n = 0;
     sh.err = 0;
     sh.overflow = 0;
   }
   __syncthreads();
-  // Union of the shards' lists.  A shard without a finite score contributes
-  // nothing; any other shard error is the row's.
-  for (int s = 0; s < m.shards; ++s) {
-    const int32_t* r;  // the row's scores; its indices follow at ids
-    const int32_t* ids;
-    int cnt, st, off = 0;
+  // Union of the shards' lists, in shard order.  A shard without a finite score
+  // contributes nothing; any other shard error is the row's.  All shards' counts
+  // and statuses are read at once, their offsets come from one scan, then every
+  // thread copies candidates of any shard: three barriers whatever the shard count.
+  int* take = sh.si;  // shard s's entries in the union (until leader_fast)
+  int* base = sh.fi;  // and where they start
+  auto shard_row = [&](int sd, const int32_t*& r, const int32_t*& ids, int& cnt, int& st, int& off) {
     if (m.blocked) {
-      const int32_t* blk = m.packed + (int64_t)s * (2 * (int64_t)m.rows * m.cap + 2 * m.rows);
+      const int32_t* blk = m.packed + (int64_t)sd * (2 * (int64_t)m.rows * m.cap + 2 * m.rows);
       r = blk + (int64_t)row * m.cap;
       ids = blk + (int64_t)m.rows * m.cap + (int64_t)row * m.cap;
       cnt = blk[2 * (int64_t)m.rows * m.cap + row];
       st = blk[2 * (int64_t)m.rows * m.cap + m.rows + row];
-      off = s * m.slice_stride;
+      off = sd * m.slice_stride;
     } else {
-      r = m.packed + ((int64_t)s * m.rows + row) * rec;
+      r = m.packed + ((int64_t)sd * m.rows + row) * rec;
       ids = r + m.cap;
       cnt = r[2 * m.cap];
       st = r[2 * m.cap + 1];
+      off = 0;
     }
-    if (st == ST_ALLNEGINF) continue;
-    if (st != ST_OK) {
-      if (tid == 0) sh.err |= 1 << st;
-      continue;
+  };
+  for (int sd = tid; sd < m.shards; sd += MNT) {
+    const int32_t *r, *ids;
+    int cnt, st, off;
+    shard_row(sd, r, ids, cnt, st, off);
+    int t = 0;
+    if (st == ST_OK) {
+      if (cnt > m.cap) atomicOr(&sh.overflow, 1);
+      t = cnt < m.cap ? cnt : m.cap;
+    } else if (st != ST_ALLNEGINF) {
+      atomicOr(&sh.err, 1 << st);
     }
-    if (cnt > m.cap && tid == 0) sh.overflow = 1;
-    const int take = cnt < m.cap ? cnt : m.cap;
-    __syncthreads();
-    const int base = sh.n;
-    for (int j = tid; j < take; j += MNT) {
-      sh.cv[base + j] = __int_as_float(r[j]);
-      sh.ci[base + j] = ids[j] + off;
+    take[sd] = t;
+  }
+  __syncthreads();
+  if (tid < 32) {  // exclusive scan of the takes, 32 shards per pass
+    int carry = 0;
+    for (int s0 = 0; s0 < m.shards; s0 += 32) {
+      const int sd = s0 + tid;
+      const int t = sd < m.shards ? take[sd] : 0;
+      int incl = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += y;
+      }
+      if (sd < m.shards) base[sd] = carry + incl - t;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    __syncthreads();
-    if (tid == 0) sh.n = base + take;
+    if (tid == 0) sh.n = carry;
+  }
+  __syncthreads();
+  for (int j = tid; j < m.shards * m.cap; j += MNT) {
+    const int sd = j / m.cap, k = j - sd * m.cap;
+    if (k >= take[sd]) continue;
+    const int32_t *r, *ids;
+    int cnt, st, off;
+    shard_row(sd, r, ids, cnt, st, off);
+    sh.cv[base[sd] + k] = __int_as_float(r[k]);
+    sh.ci[base[sd] + k] = ids[k] + off;
   }
   __syncthreads();
   const int n = sh.n;
@@ -133,6 +160,30 @@ __global__ void __launch_bounds__(MNT) merge_kernel(const MergeArgs m, const Row
   int64_t token = -1;
   if (status == ST_OK) {
     const int mm = prefilter<MNT>(sh.bs, sh.cv, sh.ci, n, a.kk, sh.fv, sh.fi);
+    if (!m.ws && mm <= 64) {
+      // Few candidates: the batched kernel's finish, two threads per candidate
+      // (its scratch over the sorted-list region, unused on this path).
+      static_assert(sizeof(SmallFin) <= sizeof(float) * kMergeMax, "the small finish's state lies over sv");
+      float mx = tid < mm ? sh.fv[tid] : Elem<float>::neg_inf();
+      mx = warp_max_nan(mx);
+      if ((tid & 31) == 0) sh.wmx[tid >> 5] = mx;
+      __syncthreads();
+      const float M = fmaxf(sh.wmx[0], sh.wmx[1]);
+      int64_t tok = -1;
+      const Kept kp = finish_small<MNT>(a, sh.fv, sh.fi, mm, M, m.uniforms[row], &tok, sh.fi, sh.fv,
+                                        *reinterpret_cast<SmallFin*>(sh.sv));
+      const float Sf = fix_to_float(kp.tot);
+      for (int j = tid; j < kp.n && j < m.out_cap; j += MNT) {
+        if (m.out_idx) m.out_idx[(int64_t)row * m.out_cap + j] = sh.fi[j];
+        if (m.out_prob) m.out_prob[(int64_t)row * m.out_cap + j] = __fdiv_rn(sv_exp(__fsub_rn(sh.fv[j], kp.M)), Sf);
+      }
+      if (tid == 0) {
+        m.out_token[row] = tok;
+        if (m.out_count) m.out_count[row] = kp.n;
+        if (m.out_status) m.out_status[row] = ST_OK;
+      }
+      return;
+    }
     int* kidx = sh.ci;
     float* kval = sh.cv;
     kept = leader_fast<MNT>(a, sh.bs, sh.fv, sh.fi, mm, sh.sv, sh.si, reinterpret_cast<uint64_t*>(sh.fv),
