@@ -790,7 +790,7 @@ __global__ void __launch_bounds__(NT, min_blocks<NT>()) stream_kernel(const RowA
 // whatever the row count.
 int threads_for(int rows, int sms) {
   if (rows >= sms * 6) return 128;
-  if (rows >= sms * 3) return 256;
+  if (rows >= sms) return 256;  // 256 rows (config 5): 256 threads beat 512 by ~1 us
   return 512;
 }
 
