@@ -23,6 +23,13 @@ def pytest_configure(config):
 
 @pytest.fixture(scope="session")
 def sv():
-    """The product package (comfyui-starvector-gguf_b200) loaded as `starvector_b200`."""
+    """The product package (comfyui-starvector-gguf_b200) loaded as `starvector_b200`;
+    the C library and its torch extension are built first when either is missing
+    (a fresh checkout)."""
+    import glob
+
     import __graft_entry__
+    pkg = __graft_entry__.PKG_DIR
+    if not (os.path.exists(os.path.join(pkg, "libstarvector_sampling.so")) and glob.glob(os.path.join(pkg, "sv_torch*.so"))):
+        __graft_entry__.build()
     return __graft_entry__.load_package()
