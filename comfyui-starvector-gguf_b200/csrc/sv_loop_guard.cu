@@ -4,14 +4,15 @@
 // occur at least `repeats` times (overlapping starts allowed, the tail itself
 // counted).
 //
-// Rows with a stride go to loop_guard_scan_kernel: a cluster of P CTAs per row,
-// each streaming its share of the row's window starts in 16-byte vectors (all of
-// a thread's loads of a pass in flight at once) and comparing every start's first
-// token with the tail's first token, the reference's own filter (:163).  The few
-// candidates of a pass are then verified against the whole tail, one warp per
-// candidate, from L2.  The CTAs' counts meet in rank 0 through distributed shared
-// memory.  The work per row is one compare per token plus the verifications, so
-// the kernel runs at the speed of the loads.
+// Rows with a stride are streamed: every window start's first token is compared
+// with the tail's first token, the reference's own filter (:163), over 16-byte
+// vector loads (all of a thread's loads of a pass in flight at once), and the few
+// candidates are then verified against the whole tail, one warp per candidate,
+// from L2.  The work per row is one compare per token plus the verifications, so
+// the kernel runs at the speed of the loads.  A row of at most one pass (16384
+// int32 tokens) is one 1024-thread CTA (loop_guard_row_kernel); longer rows are
+// split across a cluster of up to 8 CTAs whose counts meet in rank 0 through
+// distributed shared memory (loop_guard_scan_kernel).
 //
 // With row stride 0 (rows given by lengths only) loop_guard_kernel takes the rows:
 // one CTA per row.  Tokens are staged chunk by chunk in shared memory;
@@ -226,9 +227,95 @@ __global__ void __cluster_dims__(P, 1, 1) __launch_bounds__(LS_NT, sizeof(Tok) =
   if (part == 0 && tid == 0) verdict[row] = total >= repeats;
 }
 
+
+constexpr int LR_NT = 1024;
+
+// Rows of at most one pass (a 16384-token int32 row, 8192 int64): one CTA of 1024
+// threads per row, the whole row's loads in flight at once, no cluster.  The
+// candidates (at most one per position) go to dynamic shared memory.
+template <typename Tok>
+__global__ void __launch_bounds__(LR_NT, 2)
+    loop_guard_row_kernel(const Tok* __restrict__ tokens, int64_t stride, const int32_t* __restrict__ lengths,
+                          int w, int repeats, uint8_t* __restrict__ verdict) {
+  constexpr int VE = 16 / (int)sizeof(Tok);
+  constexpr int NWARP = LR_NT / 32;
+  constexpr unsigned FULL = 0xffffffffu;
+  __shared__ Tok tail[LG_MAXW];
+  extern __shared__ int cand[];
+  __shared__ int ncand, count;
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const Tok* t = tokens + row * stride;
+  const int S = (int)stride;
+  const bool vec = (reinterpret_cast<uintptr_t>(t) & 15) == 0;
+  Tok v[LS_U][VE];
+#pragma unroll
+  for (int u = 0; u < LS_U; ++u) {
+    const int pos = (u * LR_NT + tid) * VE;
+    if (vec && pos + VE <= S) {
+      const uint4 q = *reinterpret_cast<const uint4*>(t + pos);
+      memcpy(&v[u][0], &q, 16);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VE; ++j) v[u][j] = pos + j < S ? t[pos + j] : Tok(0);
+    }
+  }
+  if (tid == 0) {
+    ncand = 0;
+    count = 0;
+  }
+  int L = lengths[row];
+  if (S >= w)
+    for (int k = tid; k < w; k += LR_NT) tail[k] = t[S - w + k];
+  __syncthreads();
+  if (L > S) L = S;
+  if ((int64_t)L < (int64_t)w * repeats) {
+    if (tid == 0) verdict[row] = 0;
+    return;
+  }
+  if (L != S) {
+    for (int k = tid; k < w; k += LR_NT) tail[k] = t[L - w + k];
+    __syncthreads();
+  }
+  const int nst = L - w + 1;
+  const Tok t0 = tail[0];
+#pragma unroll
+  for (int u = 0; u < LS_U; ++u) {
+    const int pos = (u * LR_NT + tid) * VE;
+#pragma unroll
+    for (int j = 0; j < VE; ++j)
+      if (v[u][j] == t0 && pos + j < nst) cand[atomicAdd(&ncand, 1)] = pos + j;
+  }
+  __syncthreads();
+  const int nc = ncand;
+  for (int c = warp; c < nc; c += NWARP) {
+    int done = lane == 0 ? *reinterpret_cast<volatile int*>(&count) >= repeats : 0;
+    if (__shfl_sync(FULL, done, 0)) break;
+    const int st = cand[c];
+    bool eq = true;
+    for (int k = lane; k < w && eq; k += 32) eq = t[st + k] == tail[k];
+    if (__all_sync(FULL, eq) && lane == 0) atomicAdd(&count, 1);
+  }
+  __syncthreads();
+  if (tid == 0) verdict[row] = count >= repeats;
+}
+
 template <typename Tok>
 cudaError_t launch_scan(const Tok* tokens, int rows, int64_t stride, const int32_t* lengths, int window, int repeats,
                         uint8_t* verdict, cudaStream_t stream) {
+  constexpr int RPASS = LR_NT * LS_U * (16 / (int)sizeof(Tok));
+  if (stride <= RPASS) {
+    const size_t smem = (size_t)RPASS * sizeof(int);
+    static int configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaFuncSetAttribute(loop_guard_row_kernel<Tok>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      configured[dev] = 1;
+    }
+    loop_guard_row_kernel<Tok><<<rows, LR_NT, smem, stream>>>(tokens, stride, lengths, window, repeats, verdict);
+    return cudaGetLastError();
+  }
   // CTAs per row: about one pass of window starts each, at most 8 (a portable cluster).
   constexpr int PASS = LS_NT * LS_U * (16 / (int)sizeof(Tok));
   const int64_t want = (stride + PASS - 1) / PASS;
