@@ -231,18 +231,19 @@ __global__ void __cluster_dims__(P, 1, 1) __launch_bounds__(LS_NT, sizeof(Tok) =
 constexpr int LR_NT = 1024;
 
 // Rows of at most one pass (a 16384-token int32 row, 8192 int64): one CTA of 1024
-// threads per row, the whole row's loads in flight at once, no cluster.  The
-// candidates (at most one per position) go to dynamic shared memory.
+// threads per row, the whole row's loads in flight at once, no cluster, one block
+// barrier.  Each warp keeps its own candidates (at most one per position it loaded)
+// in its region of dynamic shared memory and checks them itself.
 template <typename Tok>
 __global__ void __launch_bounds__(LR_NT, 2)
     loop_guard_row_kernel(const Tok* __restrict__ tokens, int64_t stride, const int32_t* __restrict__ lengths,
                           int w, int repeats, uint8_t* __restrict__ verdict) {
   constexpr int VE = 16 / (int)sizeof(Tok);
   constexpr int NWARP = LR_NT / 32;
+  constexpr int WCAP = 32 * LS_U * VE;  // positions a warp covers: its candidates' room
   constexpr unsigned FULL = 0xffffffffu;
-  __shared__ Tok tail[LG_MAXW];
   extern __shared__ int cand[];
-  __shared__ int ncand, count;
+  __shared__ int wcount[NWARP];
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const Tok* t = tokens + row * stride;
@@ -260,44 +261,47 @@ __global__ void __launch_bounds__(LR_NT, 2)
       for (int j = 0; j < VE; ++j) v[u][j] = pos + j < S ? t[pos + j] : Tok(0);
     }
   }
-  if (tid == 0) {
-    ncand = 0;
-    count = 0;
-  }
   int L = lengths[row];
-  if (S >= w)
-    for (int k = tid; k < w; k += LR_NT) tail[k] = t[S - w + k];
-  __syncthreads();
+  Tok t0 = S >= w ? t[S - w] : Tok(0);  // the tail's first token of a full row, beside the loads
   if (L > S) L = S;
   if ((int64_t)L < (int64_t)w * repeats) {
     if (tid == 0) verdict[row] = 0;
     return;
   }
-  if (L != S) {
-    for (int k = tid; k < w; k += LR_NT) tail[k] = t[L - w + k];
-    __syncthreads();
-  }
+  if (L != S) t0 = t[L - w];
   const int nst = L - w + 1;
-  const Tok t0 = tail[0];
+  // Each warp's candidates (its own region; ballots, no block atomics), checked by
+  // the warp itself against the tail read from L2.
+  int* wc = cand + warp * WCAP;
+  int nc = 0;
 #pragma unroll
   for (int u = 0; u < LS_U; ++u) {
     const int pos = (u * LR_NT + tid) * VE;
 #pragma unroll
-    for (int j = 0; j < VE; ++j)
-      if (v[u][j] == t0 && pos + j < nst) cand[atomicAdd(&ncand, 1)] = pos + j;
+    for (int j = 0; j < VE; ++j) {
+      const bool hit = v[u][j] == t0 && pos + j < nst;
+      const unsigned bal = __ballot_sync(FULL, hit);
+      if (hit) wc[nc + __popc(bal & ((1u << lane) - 1u))] = pos + j;
+      nc += __popc(bal);
+    }
   }
-  __syncthreads();
-  const int nc = ncand;
-  for (int c = warp; c < nc; c += NWARP) {
-    int done = lane == 0 ? *reinterpret_cast<volatile int*>(&count) >= repeats : 0;
-    if (__shfl_sync(FULL, done, 0)) break;
-    const int st = cand[c];
+  __syncwarp();
+  int count = 0;
+  const Tok* tail = t + (L - w);
+  for (int c = 0; c < nc && count < repeats; ++c) {
+    const int st = wc[c];
     bool eq = true;
     for (int k = lane; k < w && eq; k += 32) eq = t[st + k] == tail[k];
-    if (__all_sync(FULL, eq) && lane == 0) atomicAdd(&count, 1);
+    count += __all_sync(FULL, eq);
   }
+  if (lane == 0) wcount[warp] = count;
   __syncthreads();
-  if (tid == 0) verdict[row] = count >= repeats;
+  if (tid == 0) {
+    int total = 0;
+#pragma unroll
+    for (int k = 0; k < NWARP; ++k) total += wcount[k];
+    verdict[row] = total >= repeats;
+  }
 }
 
 template <typename Tok>
