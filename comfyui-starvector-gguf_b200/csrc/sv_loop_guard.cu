@@ -379,13 +379,13 @@ int loop_guard_max_window() { return LG_MAXW; }
 // its positions k, three shuffles add the group's sums: the hash is a sum mod 2^32,
 // so the order does not matter), then entered together.  More windows (a table
 // built in one call) are hashed by contiguous runs per thread, the first window
-// directly and the rest rolled.  Warp 0 then reads the tail hash's probe chain 32
-// slots per load and verifies each hash match against the tail token by token
-// (the tail's own entry counts without a check), until `repeats` distinct starts
-// match (the tail itself among them, as the reference counts it) or an empty slot
-// ends the chain.
+// directly and the rest rolled.  The tail's occurrences are counted until
+// `repeats` distinct starts match (the tail itself among them, as the reference
+// counts it): among this call's windows straight from shared memory, among the
+// older ones through the table's probe chain, read 32 slots per load, each hash
+// match verified token by token (the tail's own entry counts without a check).
 
-constexpr int GI_NT = 128;
+constexpr int GI_NT = 160;  // warp 0 counts while four warps enter 16 windows per pass
 constexpr int GI_DIRECT = 256;
 
 __device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
@@ -421,20 +421,90 @@ __global__ void __launch_bounds__(GI_NT) guard_incremental_kernel(unsigned long 
   for (int j = tid; j < slen; j += GI_NT) stage[j] = tokens[s0 + j];
   for (int k = tid; k < w; k += GI_NT) pw[k] = guard_pow(kGuardBase, w - 1 - k);
   __syncthreads();
-  if (direct) {
-    // Eight lanes per window, 16 windows per pass; the loop test is warp-uniform.
-    const int g = lane >> 3, gl = lane & 7;
-    for (int64_t e = e0 + warp * 4 + g; e - g < L; e += NWARP * 4) {
-      const bool act = e < L;
-      uint32_t h = 0;
-      if (act) {
-        const int o = (int)(e - w + 1 - s0);
-        for (int k = gl; k < w; k += 8) h += guard_tok(stage[o + k]) * pw[k];
+  const Tok* tail = stage + (slen - w);
+  const bool judged = L >= (int64_t)w * repeats;
+  // Warp 0's count of the tail's occurrences among the windows whose start lies
+  // below `upto`, from the table: it reads the tail hash's probe chain 32 slots per
+  // load and verifies each hash match token by token (the tail's own entry counts
+  // without a check).
+  auto probe = [&](int64_t upto, int count) {
+    uint32_t ht = 0;
+    for (int k = lane; k < w; k += 32) ht += guard_tok(tail[k]) * pw[k];
+    ht = warp_sum_u32(ht);
+    const uint32_t self = (uint32_t)(L - w);
+    const int64_t slot0 = guard_mix(ht) & mask;
+    for (int64_t i0 = 0; i0 <= mask && count < repeats; i0 += 32) {
+      const unsigned long long e = i0 + lane <= mask ? table[(slot0 + i0 + lane) & mask] : kGuardEmpty;
+      const unsigned empty = __ballot_sync(0xffffffffu, e == kGuardEmpty);
+      const unsigned before = empty ? (1u << (__ffs(empty) - 1)) - 1u : 0xffffffffu;  // the chain's slots
+      unsigned cand = __ballot_sync(0xffffffffu, (uint32_t)(e >> 32) == ht) & before;
+      while (cand && count < repeats) {
+        const int c = __ffs(cand) - 1;
+        cand &= cand - 1;
+        const int64_t st = __shfl_sync(0xffffffffu, (unsigned)(e & 0xffffffffu), c);
+        if (st >= upto) continue;  // one of this call's windows: counted from shared memory
+        if (st == self) {
+          ++count;
+          continue;
+        }
+        bool eq = st + w <= L;
+        for (int k = lane; k < w && eq; k += 32) eq = tokens[st + k] == tail[k];
+        if (__all_sync(0xffffffffu, eq)) ++count;
       }
-#pragma unroll
-      for (int m = 4; m; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
-      if (act && gl == 0 && !guard_insert(table, mask, h, (uint32_t)(e - w + 1))) full = 1;
+      if (empty) break;
     }
+    return count;
+  };
+  int count = 0;
+  if (direct) {
+    // Warps 1.. enter this call's windows (eight lanes per window, 16 per pass; the
+    // loop test is warp-uniform) while warp 0 counts the tail among them straight
+    // from shared memory and probes the table for the older windows only, so the
+    // probe does not wait for the inserts.
+    const int64_t first_new = n ? e0 - w + 1 : L - w + 1;
+    if (warp > 0) {
+      const int g = lane >> 3, gl = lane & 7;
+      for (int64_t e = e0 + (warp - 1) * 4 + g; e - g < L; e += (NWARP - 1) * 4) {
+        const bool act = e < L;
+        uint32_t h = 0;
+        if (act) {
+          const int o = (int)(e - w + 1 - s0);
+          for (int k = gl; k < w; k += 8) h += guard_tok(stage[o + k]) * pw[k];
+        }
+#pragma unroll
+        for (int m = 4; m; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
+        if (act && gl == 0 && !guard_insert(table, mask, h, (uint32_t)(e - w + 1))) full = 1;
+      }
+    } else if (judged) {
+      // This call's windows hashed four at a time (eight lanes each) against the
+      // tail's hash; a match is verified token by token in shared memory.
+      uint32_t ht = 0;
+      for (int k = lane; k < w; k += 32) ht += guard_tok(tail[k]) * pw[k];
+      ht = warp_sum_u32(ht);
+      const int g = lane >> 3, gl = lane & 7;
+      for (int64_t st0 = first_new; st0 <= L - w && count < repeats; st0 += 4) {
+        const int64_t st = st0 + g;
+        const bool act = st <= L - w;
+        uint32_t h = 0;
+        if (act) {
+          const int o = (int)(st - s0);
+          for (int k = gl; k < w; k += 8) h += guard_tok(stage[o + k]) * pw[k];
+        }
+#pragma unroll
+        for (int m = 4; m; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
+        unsigned hit = __ballot_sync(0xffffffffu, act && gl == 0 && h == ht);
+        while (hit && count < repeats) {
+          const int c = __ffs(hit) - 1;
+          hit &= hit - 1;
+          const int o = (int)(st0 + (c >> 3) - s0);
+          bool eq = true;
+          for (int k = lane; k < w && eq; k += 32) eq = stage[o + k] == tail[k];
+          count += __all_sync(0xffffffffu, eq);
+        }
+      }
+      if (count < repeats) count = probe(first_new, count);
+    }
+    __syncthreads();  // every insert has finished (the status)
   } else {
     const uint32_t bw = guard_pow(kGuardBase, w);
     const int64_t per = (n + GI_NT - 1) / GI_NT;
@@ -447,40 +517,10 @@ __global__ void __launch_bounds__(GI_NT) guard_incremental_kernel(unsigned long 
         if (e + 1 < b) h = h * kGuardBase + guard_tok(tokens[e + 1]) - guard_tok(tokens[e + 1 - w]) * bw;
       }
     }
+    __syncthreads();
+    if (warp == 0 && judged) count = probe(L - w + 1, 0);
   }
-  __syncthreads();
-  if (warp != 0) return;
-  const Tok* tail = stage + (slen - w);
-  int count = 0;
-  if (L >= (int64_t)w * repeats) {
-    uint32_t ht = 0;
-    for (int k = lane; k < w; k += 32) ht += guard_tok(tail[k]) * pw[k];
-    ht = warp_sum_u32(ht);
-    // The entry (ht, L - w) is the tail's own window (every running row's windows
-    // are entered, so it is present): it counts without a check.
-    const uint32_t self = (uint32_t)(L - w);
-    const int64_t slot0 = guard_mix(ht) & mask;
-    for (int64_t i0 = 0; i0 <= mask && count < repeats; i0 += 32) {
-      const unsigned long long e = i0 + lane <= mask ? table[(slot0 + i0 + lane) & mask] : kGuardEmpty;
-      const unsigned empty = __ballot_sync(0xffffffffu, e == kGuardEmpty);
-      const unsigned before = empty ? (1u << (__ffs(empty) - 1)) - 1u : 0xffffffffu;  // the chain's slots
-      unsigned cand = __ballot_sync(0xffffffffu, (uint32_t)(e >> 32) == ht) & before;
-      while (cand && count < repeats) {
-        const int c = __ffs(cand) - 1;
-        cand &= cand - 1;
-        const int64_t s = __shfl_sync(0xffffffffu, (unsigned)(e & 0xffffffffu), c);
-        if (s == self) {
-          ++count;
-          continue;
-        }
-        bool eq = s + w <= L;
-        for (int k = lane; k < w && eq; k += 32) eq = tokens[s + k] == tail[k];
-        if (__all_sync(0xffffffffu, eq)) ++count;
-      }
-      if (empty) break;
-    }
-  }
-  if (lane == 0) {
+  if (tid == 0) {
     *verdict = count >= repeats;
     if (status) *status = full ? SV_ST_GUARD_FULL : SV_ST_OK;
   }
