@@ -98,7 +98,9 @@ _PINNED = {}
 
 def _read_block(arrays, first, last, device):
     """Host lists of rows [first, last] of device arrays (a dict), through pinned
-    buffers cached per shape and one stream synchronisation."""
+    buffers cached per shape and one stream synchronisation.  The buffers are shared
+    by every generation of the process: one generation at a time (as ComfyUI runs
+    its prompts)."""
     k = last + 1 - first
     host = {}
     for name, t in arrays.items():
