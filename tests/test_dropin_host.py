@@ -37,3 +37,31 @@ def test_cpu_logits_are_rejected_not_sampled_on_cpu(sv):
 def test_constants_match_reference(rs):
     assert (rs.TOP_K, rs.REPETITION_PENALTY, rs.LENGTH_PENALTY, rs.LOOP_WINDOW, rs.LOOP_REPEATS) == \
         (50, 3.1, -1.0, 64, 3)
+
+
+def test_candidate_nodes_end_like_the_reference_lists(rs):
+    """The beam replay holds candidates as linked nodes (token, parent node); its
+    _ends on a node must equal the reference's _ends on the token list
+    (runtime_shared.py:190-191) for every stop form: a list (matched), an empty
+    list (never matches a non-empty candidate) and a tuple (a list slice never
+    equals a tuple)."""
+    import random
+    rng = random.Random(7)
+    for stop in ([3, 4], [3], [], (3, 4), [4, 3, 4]):
+        for _ in range(300):
+            seq = [rng.choice([3, 4, 5]) for _ in range(rng.randint(1, 7))]
+            node = None
+            for t in seq:
+                node = (t, node)
+            assert rs._node_tokens(node) == seq
+            assert rs._node_tokens(node, 2) == seq[-2:]
+            for eos in (5, None, 99):
+                assert rs._node_ends(node, stop, eos) == rs._ends(seq, stop, eos), (seq, stop, eos)
+
+
+def test_guard_table_sizes(sv):
+    """The incremental loop guard's table: a power of two, at least twice the
+    windows it will hold, all bits set (empty)."""
+    for windows, want in ((1, 64), (32, 64), (33, 128), (4096, 8192), (4097, 16384)):
+        t = sv.ops.guard_table(windows, "cpu")
+        assert t.numel() == want and t.dtype == torch.int64 and bool((t == -1).all())
