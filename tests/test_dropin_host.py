@@ -65,3 +65,29 @@ def test_guard_table_sizes(sv):
     for windows, want in ((1, 64), (32, 64), (33, 128), (4096, 8192), (4097, 16384)):
         t = sv.ops.guard_table(windows, "cpu")
         assert t.numel() == want and t.dtype == torch.int64 and bool((t == -1).all())
+
+
+def test_device_reorder_detection(rs):
+    """Which decoders the beam loop reorders from device parents: one that offers
+    reorder_device; the reference's CachedDecoding (by class, with a CUDA cache of
+    the beams' rows); anything else gets the reference's reorder(list)."""
+    class WithHook:
+        def reorder_device(self, parents):
+            pass
+
+    hook = WithHook()
+    assert rs._device_reorder(hook, 2) == hook.reorder_device
+
+    class CachedDecoding:  # the reference's class name, but a CPU cache: not on the device path
+        def __init__(self):
+            self.keys = torch.zeros((2, 2, 8, 16))
+            self.values = torch.zeros_like(self.keys)
+            self.length = 4
+
+    assert rs._device_reorder(CachedDecoding(), 2) is None
+
+    class Other:
+        keys = values = None
+        length = 0
+
+    assert rs._device_reorder(Other(), 2) is None
